@@ -1,0 +1,700 @@
+// Persistent, warp-specialised BF16 GEMM for B200 (sm_100a): D = A * B^T.
+//
+// This is the GEMM candidate that replaces, behind the reference driver's
+// plan API, the CuTe DSL PersistentDenseGemmKernel / DenseGemmKernel and the
+// cuBLASLt call the reference study measures (driven by
+// src/gemm/gemm_comparison.py:2813-2876 and src/gemm/cublaslt_bridge_p35.cu:949-985;
+// candidate table gemm_comparison.py:214-265). Layout contract "TN":
+// A M x K row-major, B N x K row-major, D M x N row-major (gemm_comparison.py:2670-2691).
+//
+// One CTA per SM (1-CTA mode) or one CTA pair per two SMs (2-CTA mode,
+// tcgen05 cta_group::2), 192 threads:
+//   warp 0      TMA producer: one elected lane streams 128x64 A and Bx64 B
+//               K-slices into a ring of `kStages` 128B-swizzled SMEM slots,
+//               guarded by full/empty mbarriers.
+//   warp 1      allocates 512 TMEM columns; one elected lane (leader CTA
+//               only in 2-CTA mode) issues tcgen05.mma kind::f16 into a
+//               double-buffered 128x256 fp32 accumulator and frees ring slots
+//               with tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld 32 rows each -> bf16/fp32 -> swizzled
+//               SMEM staging -> TMA store; the accumulator buffer is handed
+//               back to the MMA warp as soon as its last columns are in
+//               registers, so the epilogue of tile i overlaps the MMAs of i+1.
+// Tiles are walked persistently in an M-grouped raster for L2 reuse.
+//
+// 2-CTA mode: the pair computes a 256x256 tile with M=256 MMAs issued by the
+// even CTA. Each CTA loads its own 128 A rows and 128 B rows (unicast TMA)
+// and signals the leader's full barrier; the leader's commits are sent to each
+// CTA's barrier separately (two unicast commits, no multicast anywhere).
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <new>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace b200 {
+
+constexpr int kBK = 64;            // K elements per ring slot (128 bytes: one swizzle atom row)
+constexpr int kBN = 256;           // MMA N: columns of D per tile
+constexpr int kRowsPerCta = 128;   // D rows per CTA per tile (TMEM lanes)
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+constexpr int kEpiBufBytes = 32 * 128;  // one warp's staging tile: 32 rows x 128 bytes
+constexpr int kTmemCols = 2 * kBN;      // double-buffered accumulator
+
+template <int kCtaGroup>
+struct GemmCfg {
+    static constexpr int kStages = kCtaGroup == 1 ? 4 : 6;
+    static constexpr int kABytes = kRowsPerCta * kBK * 2;
+    static constexpr int kBRows = kBN / kCtaGroup;
+    static constexpr int kBBytes = kBRows * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kTileM = kRowsPerCta * kCtaGroup;
+    static constexpr int kEpiOffset = kStages * kStageBytes;
+    static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
+    static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
+    static constexpr int kBarBytes = (2 * kStages + 4) * 8 + 16;
+    static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
+    static_assert(kStageBytes % 1024 == 0, "ring slots must keep 1024-byte alignment");
+    static_assert(kSmemBytes <= 232448, "exceeds the 227 KB opt-in shared memory");
+};
+
+struct GemmParams {
+    int m, n, k;
+    int num_m_blocks, num_n_blocks, num_k_blocks;
+    int num_tiles;
+    int group_m;
+    int* status;
+    unsigned long long timeout_ns;
+};
+
+// Linear tile id -> (m block, n block): M-grouped raster so that the tiles in
+// flight at one time share A rows and B rows in L2.
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mb, int& nb) {
+    const int per_group = p.group_m * p.num_n_blocks;
+    const int g = t / per_group;
+    const int first_m = g * p.group_m;
+    const int gm = min(p.group_m, p.num_m_blocks - first_m);
+    const int r = t - g * per_group;
+    mb = first_m + r % gm;
+    nb = r / gm;
+}
+
+template <int kCtaGroup, bool kOutF32>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
+    using C = GemmCfg<kCtaGroup>;
+    constexpr int kStages = C::kStages;
+    constexpr int kColsPerChunk = kOutF32 ? 32 : 64;  // output columns per 128-byte staging row
+    constexpr int kChunks = kBN / kColsPerChunk;
+    constexpr bool kPair = kCtaGroup == 2;
+
+    // Launch contract: uniform across the grid, checked before any barrier.
+    if (blockDim.x != kThreads || blockDim.y != 1 || blockDim.z != 1 ||
+        (kPair && cluster_nctarank() != 2) || (gridDim.x % kCtaGroup) != 0) {
+        if (threadIdx.x == 0) report_status(p.status, B200_DEV_BAD_LAUNCH);
+        return;
+    }
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t full0 = sbase + C::kBarOffset;
+    const uint32_t empty0 = full0 + 8 * kStages;
+    const uint32_t tfull0 = empty0 + 8 * kStages;
+    const uint32_t tempty0 = tfull0 + 16;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + (2 * kStages + 4) * 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = kPair ? cluster_ctarank() : 0;
+    const int cluster_id = blockIdx.x / kCtaGroup;
+    const int num_clusters = gridDim.x / kCtaGroup;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull0 + 8 * a, 1);
+            mbar_init(tempty0 + 8 * a, kEpiWarps * kCtaGroup);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmD);
+    }
+    if (warp == 1) {
+        tmem_alloc<kCtaGroup>(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish<kCtaGroup>();
+    }
+    tc_fence_before();
+    if constexpr (kPair) cluster_sync(); else __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (elect_one()) {
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            for (int t = cluster_id; ok && t < p.num_tiles; t += num_clusters) {
+                int mb, nb;
+                tile_coords(t, p, mb, nb);
+                const int a_row = mb * C::kTileM + static_cast<int>(rank) * kRowsPerCta;
+                const int b_row = nb * kBN + static_cast<int>(rank) * C::kBRows;
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.status, p.timeout_ns,
+                                   B200_DEV_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sa = sbase + stage * C::kStageBytes;
+                    const uint32_t sb = sa + C::kABytes;
+                    const uint32_t fb = full0 + 8 * stage;
+                    if constexpr (!kPair) {
+                        mbar_arrive_expect_tx(fb, C::kStageBytes);
+                        tma_load_2d(sa, &tmA, fb, kb * kBK, a_row);
+                        tma_load_2d(sb, &tmB, fb, kb * kBK, b_row);
+                    } else {
+                        const uint32_t leader_fb = mapa_shared(fb, 0);
+                        if (rank == 0) mbar_arrive_expect_tx(fb, 2 * C::kStageBytes);
+                        tma_load_2d_pair(sa, &tmA, leader_fb, kb * kBK, a_row);
+                        tma_load_2d_pair(sb, &tmB, leader_fb, kb * kBK, b_row);
+                    }
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // --------------------------------------------------------- MMA issuer
+        if (rank == 0 && elect_one()) {
+            constexpr uint32_t idesc = idesc_bf16_f32(kRowsPerCta * kCtaGroup, kBN);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (int t = cluster_id; ok && t < p.num_tiles; t += num_clusters) {
+                if (!mbar_wait<kPair>(tempty0 + 8 * acc, acc_phase ^ 1, p.status, p.timeout_ns,
+                                      B200_DEV_TIMEOUT_MMA_TMEM)) {
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kBN;
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(full0 + 8 * stage, phase, p.status, p.timeout_ns,
+                                   B200_DEV_TIMEOUT_MMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = sbase + stage * C::kStageBytes;
+                    const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k) {
+                        umma_bf16<kCtaGroup>(d_tmem, smem_desc_sw128(sa + 32 * k),
+                                             smem_desc_sw128(sb + 32 * k), idesc,
+                                             (kb | k) != 0 ? 1u : 0u);
+                    }
+                    const uint32_t eb = empty0 + 8 * stage;
+                    if constexpr (!kPair) {
+                        umma_commit<1>(eb);
+                    } else {
+                        umma_commit<2>(mapa_shared(eb, 0));
+                        umma_commit<2>(mapa_shared(eb, 1));
+                    }
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+                const uint32_t tb = tfull0 + 8 * acc;
+                if constexpr (!kPair) {
+                    umma_commit<1>(tb);
+                } else {
+                    umma_commit<2>(mapa_shared(tb, 0));
+                    umma_commit<2>(mapa_shared(tb, 1));
+                }
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+            }
+        }
+        __syncwarp();
+    } else {
+        // ----------------------------------------------------------- epilogue
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const uint32_t stage_buf0 = sbase + C::kEpiOffset + q * 2 * kEpiBufBytes;
+        uint32_t acc = 0, acc_phase = 0, buf = 0;
+        for (int t = cluster_id; t < p.num_tiles; t += num_clusters) {
+            int mb, nb;
+            tile_coords(t, p, mb, nb);
+            if (!mbar_wait<kPair>(tfull0 + 8 * acc, acc_phase, p.status, p.timeout_ns,
+                                  B200_DEV_TIMEOUT_EPILOGUE)) {
+                break;
+            }
+            tc_fence_after();
+            const int row0 = mb * C::kTileM + static_cast<int>(rank) * kRowsPerCta + q * 32;
+            const int col0 = nb * kBN;
+            const uint32_t t_row = tmem_base + acc * kBN + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < kChunks; ++c) {
+                uint32_t packed[32];
+                if constexpr (kOutF32) {
+                    tmem_ld_32x32b_x32(t_row + c * 32, packed);
+                    tmem_ld_wait();
+                } else {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld_32x32b_x32(t_row + c * 64, r0);
+                    tmem_ld_32x32b_x32(t_row + c * 64 + 32, r1);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        packed[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+                        packed[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+                    }
+                }
+                if (c == kChunks - 1) {
+                    // Accumulator fully read: hand it back before the last stores.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if constexpr (!kPair) mbar_arrive(tempty0 + 8 * acc);
+                        else mbar_arrive_cluster(mapa_shared(tempty0 + 8 * acc, 0));
+                    }
+                }
+                const uint32_t sbuf = stage_buf0 + buf * kEpiBufBytes;
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
+                const uint32_t row_addr = sbuf + lane * 128;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), packed[4 * j], packed[4 * j + 1],
+                                 packed[4 * j + 2], packed[4 * j + 3]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                const int col = col0 + c * kColsPerChunk;
+                if (lane == 0 && row0 < p.m && col < p.n) {
+                    tma_store_2d(&tmD, sbuf, col, row0);
+                    bulk_commit_group();
+                }
+                buf ^= 1;
+            }
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+        if (lane == 0) bulk_wait_group<0>();
+        __syncwarp();
+    }
+
+    // Teardown: every role is done with TMEM and with the peer's barriers.
+    tc_fence_before();
+    if constexpr (kPair) cluster_sync(); else __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc<kCtaGroup>(tmem_base, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmParams);
+
+template <int kCtaGroup, bool kOutF32>
+static KernelFn kernel_ptr() {
+    return reinterpret_cast<KernelFn>(&gemm_tn_sm100_kernel<kCtaGroup, kOutF32>);
+}
+
+static const void* kernel_sym(int cta_group, bool f32) {
+    if (cta_group == 1) {
+        return f32 ? reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<1, true>)
+                   : reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<1, false>);
+    }
+    return f32 ? reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<2, true>)
+               : reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<2, false>);
+}
+
+static int smem_bytes_for(int cta_group) {
+    return cta_group == 1 ? GemmCfg<1>::kSmemBytes : GemmCfg<2>::kSmemBytes;
+}
+
+}  // namespace b200
+
+struct B200Plan {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int cta_group = 1;
+    bool out_f32 = false;
+    CUtensorMap tmA{}, tmB{}, tmD{};
+    b200::GemmParams params{};
+    int grid = 0;
+    int smem = 0;
+    int* d_status = nullptr;
+    bool empty_problem = false;
+    B200PlanInfo info{};
+};
+
+namespace b200 {
+
+static int check_shape(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dtype, int mode) {
+    if (out_dtype != B200_OUT_BF16 && out_dtype != B200_OUT_F32) {
+        set_error("out_dtype=%d is neither B200_OUT_BF16 nor B200_OUT_F32", out_dtype);
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (mode != B200_MODE_AUTO && mode != B200_MODE_1CTA && mode != B200_MODE_2CTA) {
+        set_error("mode=%d is not one of AUTO(0), 1CTA(1), 2CTA(2)", mode);
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (m < 0 || n < 0 || k < 0) {
+        set_error("(M,N,K)=(%lld,%lld,%lld): extents must be non-negative", (long long)m,
+                  (long long)n, (long long)k);
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    const int64_t kMax = (int64_t(1) << 31) - 1;
+    if (m > kMax || n > kMax || k > kMax) {
+        set_error("(M,N,K)=(%lld,%lld,%lld): every extent must be below 2^31", (long long)m,
+                  (long long)n, (long long)k);
+        return B200_ERR_UNSUPPORTED;
+    }
+    if (k % 8 != 0) {
+        set_error("K=%lld: rows of A and B must be whole 16-byte units for TMA (K %% 8 == 0)",
+                  (long long)k);
+        return B200_ERR_UNSUPPORTED;
+    }
+    if (ldd < n) {
+        set_error("ldd=%lld is smaller than N=%lld", (long long)ldd, (long long)n);
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    const int64_t elem = out_dtype == B200_OUT_F32 ? 4 : 2;
+    if ((ldd * elem) % 16 != 0) {
+        set_error("ldd=%lld: the row pitch of D (%lld bytes) must be a multiple of 16 bytes",
+                  (long long)ldd, (long long)(ldd * elem));
+        return B200_ERR_UNSUPPORTED;
+    }
+    return B200_OK;
+}
+
+static int resolve_mode(int mode, int64_t m) {
+    if (mode != B200_MODE_AUTO) return mode;
+    return m >= 256 ? B200_MODE_2CTA : B200_MODE_1CTA;
+}
+
+static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
+                       int64_t ldd, int out_dtype, int mode, void* stream, B200Plan** out_plan,
+                       B200PlanInfo* out_info) {
+    if (out_plan == nullptr) {
+        set_error("out_plan must not be NULL");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    *out_plan = nullptr;
+    if (out_info != nullptr) std::memset(out_info, 0, sizeof(*out_info));
+    int rc = check_shape(m, n, k, ldd, out_dtype, mode);
+    if (rc != B200_OK) return rc;
+    const bool empty = (m == 0 || n == 0);
+    if (!empty && (a == nullptr && k > 0)) {
+        set_error("A must be a device pointer");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (!empty && ((b == nullptr && k > 0) || d == nullptr)) {
+        set_error("B and D must be device pointers");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    for (const void* ptr : {a, b, static_cast<const void*>(d)}) {
+        if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) {
+            set_error("operand pointer %p is not 16-byte aligned (TMA requirement)", ptr);
+            return B200_ERR_UNSUPPORTED;
+        }
+    }
+    if (!empty && k == 0) {
+        set_error("K=0 with a non-empty output is not supported (D would be all zeros)");
+        return B200_ERR_UNSUPPORTED;
+    }
+
+    int device = 0;
+    B200_CUDA_TRY(cudaGetDevice(&device));
+    DeviceProps props;
+    rc = device_props(device, &props);
+    if (rc != B200_OK) return rc;
+    if (props.cc_major != 10 || props.cc_minor != 0) {
+        set_error("device %d has compute capability %d.%d; this library is built for sm_100a (10.0)",
+                  device, props.cc_major, props.cc_minor);
+        return B200_ERR_UNSUPPORTED;
+    }
+
+    B200Plan* plan = new (std::nothrow) B200Plan();
+    if (plan == nullptr) {
+        set_error("out of host memory");
+        return B200_ERR_INTERNAL;
+    }
+    plan->device = device;
+    plan->stream = static_cast<cudaStream_t>(stream);
+    plan->out_f32 = out_dtype == B200_OUT_F32;
+    const int resolved = resolve_mode(mode, m);
+    plan->cta_group = resolved == B200_MODE_2CTA ? 2 : 1;
+    plan->empty_problem = empty;
+
+    const int tile_m = kRowsPerCta * plan->cta_group;
+    GemmParams& p = plan->params;
+    p.m = static_cast<int>(m);
+    p.n = static_cast<int>(n);
+    p.k = static_cast<int>(k);
+    p.num_m_blocks = static_cast<int>((m + tile_m - 1) / tile_m);
+    p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
+    p.num_k_blocks = static_cast<int>((k + kBK - 1) / kBK);
+    p.num_tiles = p.num_m_blocks * p.num_n_blocks;
+    p.group_m = 16;
+    p.timeout_ns = wait_timeout_ns();
+
+    cudaError_t err = cudaMalloc(&plan->d_status, sizeof(int));
+    if (err != cudaSuccess) {
+        delete plan;
+        return cuda_fail("cudaMalloc(status word)", err);
+    }
+    err = cudaMemset(plan->d_status, 0, sizeof(int));
+    if (err != cudaSuccess) {
+        cudaFree(plan->d_status);
+        delete plan;
+        return cuda_fail("cudaMemset(status word)", err);
+    }
+    p.status = plan->d_status;
+
+    int slots = 0;
+    if (!empty) {
+        rc = encode_tmap_2d(&plan->tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, m, k, k,
+                            kRowsPerCta, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc == B200_OK)
+            rc = encode_tmap_2d(&plan->tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, n, k, k,
+                                kBN / plan->cta_group, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc == B200_OK) {
+            if (plan->out_f32)
+                rc = encode_tmap_2d(&plan->tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, m, n, ldd, 32,
+                                    32, CU_TENSOR_MAP_SWIZZLE_128B);
+            else
+                rc = encode_tmap_2d(&plan->tmD, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, m, n, ldd, 32,
+                                    64, CU_TENSOR_MAP_SWIZZLE_128B);
+        }
+        if (rc != B200_OK) {
+            cudaFree(plan->d_status);
+            delete plan;
+            return rc;
+        }
+        plan->smem = smem_bytes_for(plan->cta_group);
+        const void* sym = kernel_sym(plan->cta_group, plan->out_f32);
+        err = cudaFuncSetAttribute(sym, cudaFuncAttributeMaxDynamicSharedMemorySize, plan->smem);
+        if (err == cudaSuccess && plan->cta_group == 2)
+            err = cudaFuncSetAttribute(sym, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        if (err != cudaSuccess) {
+            cudaFree(plan->d_status);
+            delete plan;
+            return cuda_fail("cudaFuncSetAttribute", err);
+        }
+        if (plan->cta_group == 1) {
+            slots = props.sm_count;
+        } else {
+            cudaLaunchConfig_t cfg = {};
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.gridDim = dim3(props.sm_count, 1, 1);
+            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.dynamicSmemBytes = plan->smem;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int clusters = 0;
+            err = cudaOccupancyMaxActiveClusters(&clusters, sym, &cfg);
+            if (err != cudaSuccess || clusters <= 0) {
+                cudaGetLastError();
+                clusters = props.sm_count / 2;
+            }
+            slots = clusters;
+        }
+        const int clusters = std::min(p.num_tiles, slots);
+        plan->grid = clusters * plan->cta_group;
+    }
+
+    B200PlanInfo& info = plan->info;
+    info.abi_version = B200_ABI_VERSION;
+    info.m = m;
+    info.n = n;
+    info.k = k;
+    info.lda = k;
+    info.ldb = k;
+    info.ldd = ldd;
+    info.out_dtype = out_dtype;
+    info.mode = resolved;
+    info.cta_group = plan->cta_group;
+    info.tile_m = tile_m;
+    info.tile_n = kBN;
+    info.tile_k = kBK;
+    info.stages = plan->cta_group == 1 ? GemmCfg<1>::kStages : GemmCfg<2>::kStages;
+    info.cluster_m = plan->cta_group;
+    info.grid_ctas = plan->grid;
+    info.threads_per_cta = kThreads;
+    info.smem_bytes = plan->smem;
+    info.tmem_columns = kTmemCols;
+    info.num_tiles = empty ? 0 : p.num_tiles;
+    info.sm_count = props.sm_count;
+    info.device = device;
+    info.waves = (slots > 0) ? static_cast<double>(p.num_tiles) / slots : 0.0;
+    info.flop_count = 2.0 * static_cast<double>(m) * static_cast<double>(n) * static_cast<double>(k);
+    if (out_info != nullptr) *out_info = info;
+    *out_plan = plan;
+    return B200_OK;
+}
+
+static int plan_launch(B200Plan* plan, cudaStream_t stream) {
+    if (plan->empty_problem) return B200_OK;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(plan->grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = plan->smem;
+    cfg.stream = stream;
+    if (plan->cta_group == 2) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t err;
+    if (plan->cta_group == 1) {
+        if (plan->out_f32)
+            err = cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<1, true>, plan->tmA, plan->tmB, plan->tmD, plan->params);
+        else
+            err = cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<1, false>, plan->tmA, plan->tmB, plan->tmD, plan->params);
+    } else {
+        if (plan->out_f32)
+            err = cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<2, true>, plan->tmA, plan->tmB, plan->tmD, plan->params);
+        else
+            err = cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<2, false>, plan->tmA, plan->tmB, plan->tmD, plan->params);
+    }
+    if (err != cudaSuccess) return cuda_fail("cudaLaunchKernelEx(gemm_tn_sm100_kernel)", err);
+    return B200_OK;
+}
+
+}  // namespace b200
+
+extern "C" {
+
+int b200_gemm_supported(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dtype, int mode) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    return b200::check_shape(m, n, k, ldd, out_dtype, mode);
+    B200_ABI_GUARD_END
+}
+
+int b200_gemm_plan_create(int64_t m, int64_t n, int64_t k, const void* a, const void* b,
+                          const void* c, void* d, void* stream, B200Plan** out_plan,
+                          B200PlanInfo* out_info) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    (void)c;
+    return b200::plan_create(m, n, k, a, b, d, n, B200_OUT_F32, B200_MODE_AUTO, stream, out_plan,
+                             out_info);
+    B200_ABI_GUARD_END
+}
+
+int b200_gemm_plan_create_ex(int64_t m, int64_t n, int64_t k, const void* a, const void* b,
+                             void* d, int64_t ldd, int out_dtype, int mode, void* stream,
+                             B200Plan** out_plan, B200PlanInfo* out_info) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    return b200::plan_create(m, n, k, a, b, d, ldd, out_dtype, mode, stream, out_plan, out_info);
+    B200_ABI_GUARD_END
+}
+
+int b200_gemm_plan_execute(B200Plan* plan) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    if (plan == nullptr) {
+        b200::set_error("plan is NULL");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    return b200::plan_launch(plan, plan->stream);
+    B200_ABI_GUARD_END
+}
+
+int b200_gemm_plan_execute_on(B200Plan* plan, void* stream) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    if (plan == nullptr) {
+        b200::set_error("plan is NULL");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    return b200::plan_launch(plan, static_cast<cudaStream_t>(stream));
+    B200_ABI_GUARD_END
+}
+
+int b200_stream_synchronize(B200Plan* plan) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    if (plan == nullptr) {
+        b200::set_error("plan is NULL");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    B200_CUDA_TRY(cudaStreamSynchronize(plan->stream));
+    int status = 0;
+    B200_CUDA_TRY(cudaMemcpy(&status, plan->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (status != 0) {
+        B200_CUDA_TRY(cudaMemset(plan->d_status, 0, sizeof(int)));
+        b200::set_error("GEMM kernel reported device status 0x%x (%s)", status,
+                        status == B200_DEV_BAD_LAUNCH ? "launch contract violated"
+                                                      : "bounded wait timed out");
+        return status == B200_DEV_BAD_LAUNCH ? B200_ERR_INTERNAL : B200_ERR_DEVICE_TIMEOUT;
+    }
+    return B200_OK;
+    B200_ABI_GUARD_END
+}
+
+int b200_gemm_plan_destroy(B200Plan* plan) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    if (plan == nullptr) return B200_OK;
+    cudaError_t err = cudaSuccess;
+    if (plan->d_status != nullptr) err = cudaFree(plan->d_status);
+    delete plan;
+    if (err != cudaSuccess) return b200::cuda_fail("cudaFree(status word)", err);
+    return B200_OK;
+    B200_ABI_GUARD_END
+}
+
+int64_t b200_gemm_plan_launches(const B200Plan* plan) {
+    if (plan == nullptr || plan->empty_problem) return 0;
+    return 1;
+}
+
+int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d, int64_t ldd,
+              int out_dtype, int mode, void* stream) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    B200Plan* plan = nullptr;
+    int rc = b200::plan_create(m, n, k, a, b, d, ldd, out_dtype, mode, stream, &plan, nullptr);
+    if (rc != B200_OK) return rc;
+    rc = b200::plan_launch(plan, plan->stream);
+    // The status word is freed with the plan; synchronise so the launch no
+    // longer references it.
+    cudaError_t err = cudaStreamSynchronize(plan->stream);
+    int status = 0;
+    if (err == cudaSuccess) err = cudaMemcpy(&status, plan->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(plan->d_status);
+    delete plan;
+    if (rc != B200_OK) return rc;
+    if (err != cudaSuccess) return b200::cuda_fail("b200_gemm synchronize", err);
+    if (status != 0) {
+        b200::set_error("GEMM kernel reported device status 0x%x", status);
+        return B200_ERR_DEVICE_TIMEOUT;
+    }
+    return B200_OK;
+    B200_ABI_GUARD_END
+}
+
+}  // extern "C"

@@ -1,0 +1,270 @@
+/*
+ * b200gemm.h — C ABI of the B200 (sm_100a) BF16 GEMM stack.
+ *
+ * Plain C: every function returns int (0 = B200_OK) or a plain size/pointer,
+ * never lets a C++ exception cross, writes nothing to stdout/stderr, and keeps
+ * the last error message in thread-local storage (b200_last_error). Pointers
+ * are device pointers unless a comment says otherwise; `stream` is a
+ * cudaStream_t passed as void* (0 = legacy default stream).
+ *
+ * Conventions follow the reference study's cuBLASLt bridge, which this library
+ * replaces as the GEMM candidate behind the same driver:
+ *   src/gemm/cublaslt_bridge.cu:106-126   thread-local last error
+ *   src/gemm/cublaslt_bridge.cu:128-191   all-8-byte metadata struct + size handshake
+ *   src/gemm/cublaslt_bridge_p35.cu:563-1018  plan create / execute / sync / destroy
+ * Layout contract (src/gemm/gemm_comparison.py:2670-2691, cublaslt_bridge_p35.cu:96-111):
+ *   A is M x K row-major (K contiguous), B is N x K row-major (K contiguous,
+ *   "TN"), D is M x N row-major with leading dimension ldd (elements).
+ *   D = A * B^T, bf16 inputs, fp32 accumulation, beta = 0.
+ */
+#ifndef B200GEMM_H_
+#define B200GEMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_ABI_VERSION 1
+
+/* Host-side return codes. */
+enum {
+    B200_OK = 0,
+    B200_ERR_INVALID_ARGUMENT = 1,
+    B200_ERR_UNSUPPORTED = 2,
+    B200_ERR_CUDA = 3,
+    B200_ERR_DEVICE_TIMEOUT = 4, /* a kernel gave up a bounded wait; see b200_last_error */
+    B200_ERR_MISMATCH = 5,       /* a self-validating kernel found wrong data */
+    B200_ERR_NO_DEVICE = 6,
+    B200_ERR_INTERNAL = 7
+};
+
+/* Codes a kernel writes into its device status word (first failure wins). */
+enum {
+    B200_DEV_OK = 0,
+    B200_DEV_TIMEOUT_PRODUCER = 0x101, /* TMA producer waited too long for a free ring slot */
+    B200_DEV_TIMEOUT_MMA_FULL = 0x102, /* MMA issuer waited too long for operands */
+    B200_DEV_TIMEOUT_MMA_TMEM = 0x103, /* MMA issuer waited too long for a free accumulator */
+    B200_DEV_TIMEOUT_EPILOGUE = 0x104, /* epilogue waited too long for an accumulator */
+    B200_DEV_TIMEOUT_STREAM = 0x105,   /* memory-path streamer waited too long for a stage */
+    B200_DEV_TIMEOUT_UMMA = 0x106,     /* UMMA probe waited too long for its commit */
+    B200_DEV_BAD_LAUNCH = 0x1FF        /* launch geometry differs from the kernel's contract */
+};
+
+/* Output element types. */
+enum { B200_OUT_BF16 = 0, B200_OUT_F32 = 1 };
+
+/* GEMM modes. AUTO picks the pair-CTA kernel when it has enough tiles. */
+enum { B200_MODE_AUTO = 0, B200_MODE_1CTA = 1, B200_MODE_2CTA = 2 };
+
+/* ------------------------------------------------------------------------ */
+/* Library / device                                                          */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces p35_bridge_abi_version (cublaslt_bridge_p35.cu:525). */
+int b200_abi_version(void);
+/* Replaces p35_plan_info_size (cublaslt_bridge_p35.cu:530). */
+size_t b200_plan_info_size(void);
+size_t b200_device_info_size(void);
+size_t b200_stream_result_size(void);
+/* Replaces p35_last_error (cublaslt_bridge_p35.cu:535). Thread-local, never NULL. */
+const char* b200_last_error(void);
+
+typedef struct B200DeviceInfo {
+    int64_t device;
+    int64_t cc_major;
+    int64_t cc_minor;
+    int64_t sm_count;
+    int64_t l2_bytes;
+    int64_t smem_per_sm_bytes;
+    int64_t smem_optin_bytes;
+    int64_t global_mem_bytes;
+    int64_t driver_version;
+    int64_t runtime_version;
+    int64_t clock_khz;
+    int64_t is_sm100; /* 1 when the device runs this library's sm_100a code */
+} B200DeviceInfo;
+
+/* Replaces the reference's query_gpu_info (src/memory/ldgsts.cu:397-445) and
+ * the CUDA smoke binary (smoke/cuda_smoke.cu): fills *out for `device`.
+ * Returns B200_ERR_NO_DEVICE when no CUDA device is visible. */
+int b200_device_probe(int device, B200DeviceInfo* out);
+
+/* ------------------------------------------------------------------------ */
+/* GEMM plans                                                                */
+/* ------------------------------------------------------------------------ */
+
+typedef struct B200Plan B200Plan;
+
+typedef struct B200PlanInfo {
+    int64_t abi_version;
+    int64_t m;
+    int64_t n;
+    int64_t k;
+    int64_t lda;
+    int64_t ldb;
+    int64_t ldd;
+    int64_t out_dtype;      /* B200_OUT_* */
+    int64_t mode;           /* resolved B200_MODE_1CTA or B200_MODE_2CTA */
+    int64_t cta_group;      /* 1 or 2 */
+    int64_t tile_m;         /* rows of D per tile (per CTA pair in 2-CTA mode) */
+    int64_t tile_n;
+    int64_t tile_k;
+    int64_t stages;
+    int64_t cluster_m;
+    int64_t grid_ctas;
+    int64_t threads_per_cta;
+    int64_t smem_bytes;
+    int64_t tmem_columns;
+    int64_t num_tiles;
+    int64_t sm_count;
+    int64_t device;
+    double waves;           /* num_tiles / resident tile slots */
+    double flop_count;      /* 2*M*N*K */
+} B200PlanInfo;
+
+/* Reference-compatible plan: the exact argument list of p35_plan_create
+ * (src/gemm/cublaslt_bridge_p35.cu:563-572). Output D is fp32 M x N
+ * row-major, like the reference's CUDA_R_32F D; C is accepted for signature
+ * compatibility and ignored (beta = 0). Mode AUTO. */
+int b200_gemm_plan_create(int64_t m, int64_t n, int64_t k, const void* a, const void* b,
+                          const void* c, void* d, void* stream, B200Plan** out_plan,
+                          B200PlanInfo* out_info);
+
+/* Full-control plan: out_dtype B200_OUT_BF16 or B200_OUT_F32, mode B200_MODE_*,
+ * ldd >= n (elements; ldd*elem_size must be a multiple of 16 bytes). No
+ * counterpart in the reference beyond p35_plan_create; it exposes the bf16
+ * output, the mode choice and strided output placement (used to write an
+ * N-shard at its column offset inside a larger matrix). */
+int b200_gemm_plan_create_ex(int64_t m, int64_t n, int64_t k, const void* a, const void* b,
+                             void* d, int64_t ldd, int out_dtype, int mode, void* stream,
+                             B200Plan** out_plan, B200PlanInfo* out_info);
+
+/* Replaces p35_plan_execute (cublaslt_bridge_p35.cu:949): one asynchronous
+ * launch on the plan's stream. */
+int b200_gemm_plan_execute(B200Plan* plan);
+
+/* Same launch on another stream (e.g. inside a CUDA-graph capture). */
+int b200_gemm_plan_execute_on(B200Plan* plan, void* stream);
+
+/* Replaces p35_stream_synchronize (cublaslt_bridge_p35.cu:987): waits for the
+ * plan's stream, then reads and clears the device status word; a kernel that
+ * gave up a bounded wait turns into B200_ERR_DEVICE_TIMEOUT here. */
+int b200_stream_synchronize(B200Plan* plan);
+
+/* Replaces p35_plan_destroy (cublaslt_bridge_p35.cu:1008). NULL is a no-op. */
+int b200_gemm_plan_destroy(B200Plan* plan);
+
+/* Analogue of CuTe's can_implement (src/gemm/cutedsl_variants.py:1296-1324):
+ * B200_OK when the shape/dtype/mode is accepted, otherwise an error code with
+ * the reason in b200_last_error. Pointer alignment is checked at create. */
+int b200_gemm_supported(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dtype, int mode);
+
+/* One-shot GEMM: create, execute, destroy (no synchronisation). */
+int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
+              int64_t ldd, int out_dtype, int mode, void* stream);
+
+/* Number of device kernels one execute launches (for launch accounting). */
+int64_t b200_gemm_plan_launches(const B200Plan* plan);
+
+/* ------------------------------------------------------------------------ */
+/* Memory path: global -> shared streaming (LDGSTS / TMA)                     */
+/* Replaces the ldgsts and tma benchmark binaries                             */
+/* (src/memory/ldgsts.cu:273-380, src/memory/tma.cu:452-607).                 */
+/* ------------------------------------------------------------------------ */
+
+enum {
+    B200_STREAM_LDGSTS = 0,  /* 16-byte cp.async.cg, 128 threads, ring of `stages` slots */
+    B200_STREAM_TMA = 1,     /* reference geometry: box 128 x tile_h of 2-byte elements, no swizzle */
+    B200_STREAM_TMA_SW128 = 2 /* GEMM geometry: box 64 x rows bf16 (128-byte rows), 128B swizzle */
+};
+
+enum {
+    B200_STREAM_VALIDATE = 0, /* compare every 16-byte vector with the SplitMix64 pattern */
+    B200_STREAM_CHECKSUM = 1, /* XOR and wrapping sum of every 32-bit word read */
+    B200_STREAM_SINK = 2      /* timed mode of the reference: XOR one word per thread per stage */
+};
+
+typedef struct B200StreamConfig {
+    int64_t method;       /* B200_STREAM_* */
+    int64_t stages;       /* 2, 4 or 8 */
+    int64_t stage_bytes;  /* bytes per ring slot: multiple of 2048, <= 65536 */
+    int64_t ctas_per_sm;  /* 1, 2 or 4 (reference: 1) */
+    int64_t passes;       /* >= 1 */
+    int64_t rotation;     /* tile-order rotation of the first pass (reference rotation_base) */
+} B200StreamConfig;
+
+typedef struct B200StreamResult {
+    int64_t grid_ctas;
+    int64_t threads_per_cta;
+    int64_t smem_bytes;
+    int64_t occupancy_ctas_per_sm;
+    int64_t tiles_per_cta;
+    int64_t bytes_streamed;      /* working set bytes x passes */
+    int64_t mismatches;          /* VALIDATE */
+    int64_t checksum_xor;        /* CHECKSUM: XOR of all 32-bit words (zero-extended) */
+    int64_t checksum_sum;        /* CHECKSUM: sum of all 32-bit words mod 2^64, as int64 */
+    int64_t sink_xor;            /* SINK: XOR over the per-thread sink words */
+    int64_t status;              /* device status word */
+} B200StreamResult;
+
+typedef struct B200StreamPlan B200StreamPlan;
+
+/* Fills `bytes` (multiple of 16) of device memory with the reference's
+ * SplitMix64 index pattern (src/memory/ldgsts.cu:226-246). */
+int b200_fill_pattern(void* buf, int64_t bytes, void* stream);
+
+/* Creates a streaming plan over `bytes` of device memory at `buf`. The
+ * working set must split into whole stages per CTA: bytes must be a multiple
+ * of grid_ctas * stage_bytes (b200_stream_plan_granule gives that unit). */
+int b200_stream_plan_create(const B200StreamConfig* cfg, const void* buf, int64_t bytes,
+                            int device, B200StreamPlan** out_plan, B200StreamResult* out_info);
+int64_t b200_stream_plan_granule(const B200StreamConfig* cfg, int device);
+/* One asynchronous launch in mode B200_STREAM_*; clears the plan's counters first. */
+int b200_stream_plan_execute(B200StreamPlan* plan, int mode, void* stream);
+/* Synchronises `stream` and fills *out with the last launch's results. */
+int b200_stream_plan_result(B200StreamPlan* plan, void* stream, B200StreamResult* out);
+int b200_stream_plan_destroy(B200StreamPlan* plan);
+
+/* ------------------------------------------------------------------------ */
+/* UMMA throughput probe (tcgen05.mma kind::f16, operands resident in SMEM)  */
+/* Replaces umma_1sm_m128n{N}k16_d{DEPTH} (src/compute/umma_1sm.cu:520-538)  */
+/* and umma_2sm_m256n{N}k16_d{DEPTH} (src/compute/umma_2sm.cu:733-737).      */
+/* ------------------------------------------------------------------------ */
+
+typedef struct B200UmmaConfig {
+    int64_t cta_group;   /* 1 (M = 128, one CTA) or 2 (M = 256, one CTA pair) */
+    int64_t n;           /* 64, 128 or 256 */
+    int64_t depth;       /* MMAs of K = 16 per commit: 4, 16, 32, 64, 128 or 256 */
+    int64_t iterations;  /* commit+wait rounds, >= 1 */
+    int64_t timed;       /* 1: leader thread reads %clock64 around the loop */
+    int64_t num_ctas;    /* 0: one CTA (pair); else that many CTAs (pairs x2) in parallel */
+} B200UmmaConfig;
+
+/* Runs the probe. a (M x 16 bf16, row-major) and b (N x 16 bf16, row-major)
+ * may be NULL, which selects the reference's integer pattern
+ * A[r,k] = ((r+3k) mod 7) - 3, B[k,c] = ((2k+c) mod 5) - 2 on global rows/cols.
+ * d_out receives D of the first CTA (pair): M x N fp32 row-major, which equals
+ * depth * A * B^T. cycles (device, one uint64 per CTA) receives the leader's
+ * %clock64 delta when timed. status (device int) receives B200_DEV_* codes. */
+int b200_umma_probe(const B200UmmaConfig* cfg, const void* a, const void* b, float* d_out,
+                    unsigned long long* cycles, int* status, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Multi-GPU N-sharding (host arithmetic; the collective runs in the caller) */
+/* ------------------------------------------------------------------------ */
+
+/* Column range [*n_begin, *n_end) of output shard `rank` of `world` for an
+ * N-column GEMM: shards are ceil(N/world) rounded up to `granule` columns,
+ * the last one takes the remainder (possibly empty). No counterpart in the
+ * reference (it has no multi-GPU path). */
+int b200_shard_range(int64_t n, int64_t world, int64_t rank, int64_t granule, int64_t* n_begin,
+                     int64_t* n_end);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200GEMM_H_ */
