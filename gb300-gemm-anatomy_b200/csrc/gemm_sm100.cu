@@ -698,3 +698,156 @@ int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, voi
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// b200_gemm_noalloc runs the same kernel as b200_gemm, but the one piece of
+// device scratch the kernel needs -- its status word, where bounded waits
+// record a timeout -- lives in the file-scope array below instead of a
+// cudaMalloc'd buffer. Callers that cannot allocate device memory use it:
+// applications that hand all device memory to their own pool at start-up and
+// forbid later driver allocations, and latency-critical paths that must not
+// take the implicit device-wide synchronisation cudaMalloc/cudaFree imply.
+// ---------------------------------------------------------------------------
+namespace b200 {
+
+constexpr size_t kNoAllocScratchBytes = 256;  // stated maximum of the static scratch
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on `device`. In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per
+// device with that device current and cached.
+static int noalloc_scratch_address(int device, void** out) {
+    constexpr int kMaxDevices = 64;
+    static void* addr[kMaxDevices] = {};
+    static std::mutex mu;
+    if (device < 0 || device >= kMaxDevices) {
+        set_error("device index %d out of range", device);
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[device] == nullptr) {
+        int current = -1;
+        B200_CUDA_TRY(cudaGetDevice(&current));
+        if (current != device) B200_CUDA_TRY(cudaSetDevice(device));
+        void* p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (current != device) cudaSetDevice(current);
+        if (err != cudaSuccess) return cuda_fail("cudaGetSymbolAddress(g_noalloc_scratch)", err);
+        addr[device] = p;
+    }
+    *out = addr[device];
+    return B200_OK;
+}
+
+// Fills `plan` like plan_create, without any allocation; the status word is
+// `status` (a pointer into the static scratch).
+static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, const void* a,
+                           const void* b, void* d, int64_t ldd, int out_dtype, int mode,
+                           int device, const DeviceProps& props, int* status) {
+    plan->device = device;
+    plan->out_f32 = out_dtype == B200_OUT_F32;
+    plan->cta_group = resolve_mode(mode, m) == B200_MODE_2CTA ? 2 : 1;
+    plan->empty_problem = (m == 0 || n == 0);
+    plan->d_status = status;
+    const int tile_m = kRowsPerCta * plan->cta_group;
+    GemmParams& p = plan->params;
+    p.m = static_cast<int>(m);
+    p.n = static_cast<int>(n);
+    p.k = static_cast<int>(k);
+    p.num_m_blocks = static_cast<int>((m + tile_m - 1) / tile_m);
+    p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
+    p.num_k_blocks = static_cast<int>((k + kBK - 1) / kBK);
+    p.num_tiles = p.num_m_blocks * p.num_n_blocks;
+    p.group_m = 16;
+    p.timeout_ns = wait_timeout_ns();
+    p.status = status;
+    if (plan->empty_problem) return B200_OK;
+    int rc = encode_tmap_2d(&plan->tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, m, k, k,
+                            kRowsPerCta, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == B200_OK)
+        rc = encode_tmap_2d(&plan->tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, n, k, k,
+                            kBN / plan->cta_group, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == B200_OK)
+        rc = plan->out_f32
+                 ? encode_tmap_2d(&plan->tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, m, n, ldd, 32, 32,
+                                  CU_TENSOR_MAP_SWIZZLE_128B)
+                 : encode_tmap_2d(&plan->tmD, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, m, n, ldd, 32, 64,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != B200_OK) return rc;
+    plan->smem = smem_bytes_for(plan->cta_group);
+    const void* sym = kernel_sym(plan->cta_group, plan->out_f32);
+    B200_CUDA_TRY(cudaFuncSetAttribute(sym, cudaFuncAttributeMaxDynamicSharedMemorySize, plan->smem));
+    // One CTA (pair) per SM (pair); the persistent kernel needs no more.
+    const int slots = plan->cta_group == 1 ? props.sm_count : props.sm_count / 2;
+    plan->grid = std::min(p.num_tiles, std::max(slots, 1)) * plan->cta_group;
+    return B200_OK;
+}
+
+}  // namespace b200
+
+extern "C" int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a, const void* b,
+                                 void* d, int64_t ldd, int out_dtype, int mode, void* stream) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    int rc = b200::check_shape(m, n, k, ldd, out_dtype, mode);
+    if (rc != B200_OK) return rc;
+    const bool empty = (m == 0 || n == 0);
+    if (!empty && (a == nullptr || b == nullptr || d == nullptr)) {
+        b200::set_error("A, B and D must be device pointers");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    for (const void* ptr : {a, b, static_cast<const void*>(d)}) {
+        if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) {
+            b200::set_error("operand pointer %p is not 16-byte aligned (TMA requirement)", ptr);
+            return B200_ERR_UNSUPPORTED;
+        }
+    }
+    if (!empty && k == 0) {
+        b200::set_error("K=0 with a non-empty output is not supported (D would be all zeros)");
+        return B200_ERR_UNSUPPORTED;
+    }
+    // This launch needs one status word of scratch; refuse anything that would
+    // not fit the static array.
+    constexpr size_t kNeeded = sizeof(int);
+    if (kNeeded > b200::kNoAllocScratchBytes) {
+        b200::set_error("b200_gemm_noalloc needs %zu bytes of scratch, the static array holds %zu",
+                        kNeeded, b200::kNoAllocScratchBytes);
+        return B200_ERR_UNSUPPORTED;
+    }
+    int device = 0;
+    B200_CUDA_TRY(cudaGetDevice(&device));
+    b200::DeviceProps props;
+    rc = b200::device_props(device, &props);
+    if (rc != B200_OK) return rc;
+    if (props.cc_major != 10 || props.cc_minor != 0) {
+        b200::set_error("device %d has compute capability %d.%d; this library is built for sm_100a (10.0)",
+                        device, props.cc_major, props.cc_minor);
+        return B200_ERR_UNSUPPORTED;
+    }
+    void* scratch = nullptr;
+    rc = b200::noalloc_scratch_address(device, &scratch);
+    if (rc != B200_OK) return rc;
+    int* status = static_cast<int*>(scratch);
+
+    B200Plan plan;  // on the stack: no host or device allocation
+    plan.stream = static_cast<cudaStream_t>(stream);
+    rc = b200::noalloc_prepare(&plan, m, n, k, a, b, d, ldd, out_dtype, mode, device, props, status);
+    if (rc != B200_OK) return rc;
+    if (plan.empty_problem) return B200_OK;
+
+    // The array keeps the previous call's contents: the status word must start at zero.
+    B200_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), plan.stream));
+    rc = b200::plan_launch(&plan, plan.stream);
+    if (rc != B200_OK) return rc;
+    int host_status = 0;
+    B200_CUDA_TRY(cudaMemcpyAsync(&host_status, status, sizeof(int), cudaMemcpyDeviceToHost, plan.stream));
+    B200_CUDA_TRY(cudaStreamSynchronize(plan.stream));
+    if (host_status != 0) {
+        b200::set_error("GEMM kernel reported device status 0x%x", host_status);
+        return host_status == B200_DEV_BAD_LAUNCH ? B200_ERR_INTERNAL : B200_ERR_DEVICE_TIMEOUT;
+    }
+    return B200_OK;
+    B200_ABI_GUARD_END
+}

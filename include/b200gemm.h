@@ -162,9 +162,26 @@ int b200_gemm_plan_destroy(B200Plan* plan);
  * the reason in b200_last_error. Pointer alignment is checked at create. */
 int b200_gemm_supported(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dtype, int mode);
 
-/* One-shot GEMM: create, execute, destroy (no synchronisation). */
+/* One-shot GEMM: create, execute, synchronise, check the status word, destroy. */
 int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
               int64_t ldd, int out_dtype, int mode, void* stream);
+
+/* Allocation-free GEMM. No counterpart in the reference. Same arguments,
+ * kernel and synchronous behaviour as b200_gemm, but it calls no cudaMalloc,
+ * cudaFree or other allocating routine: the kernel's only scratch (its 4-byte
+ * status word for bounded-wait timeouts) lives in a 256-byte static device
+ * array of the library, which every GPU that loads the library holds until
+ * exit. For callers that cannot allocate device memory -- programs that give
+ * all device memory to their own pool up front, or paths that must avoid the
+ * device-wide synchronisation cudaMalloc/cudaFree imply.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. Calls
+ * share the array: each clears the status word before its launch, and calls
+ * that overlap on the GPU (other streams, other threads) race on it. A launch
+ * whose scratch need exceeded the array would be refused with
+ * B200_ERR_UNSUPPORTED; this kernel needs 4 bytes whatever M, N and K are. */
+int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
+                      int64_t ldd, int out_dtype, int mode, void* stream);
 
 /* Number of device kernels one execute launches (for launch accounting). */
 int64_t b200_gemm_plan_launches(const B200Plan* plan);
