@@ -46,6 +46,7 @@ DEV_STATUS_NAMES = {
     0x104: "TIMEOUT_EPILOGUE",
     0x105: "TIMEOUT_STREAM",
     0x106: "TIMEOUT_UMMA",
+    0x107: "TIMEOUT_SELFTEST",
     0x1FF: "BAD_LAUNCH",
 }
 
@@ -131,6 +132,7 @@ SIGNATURES = {
     "b200_stream_plan_result": (_INT, [_P, _P, ctypes.POINTER(StreamResult)]),
     "b200_stream_plan_destroy": (_INT, [_P]),
     "b200_umma_probe": (_INT, [ctypes.POINTER(UmmaConfig), _P, _P, _P, _P, _P, _P]),
+    "b200_selftest_bounded_wait": (_INT, [ctypes.c_ulonglong, _P, _P]),
     "b200_shard_range": (_INT, [_I64, _I64, _I64, _I64, ctypes.POINTER(_I64),
                                 ctypes.POINTER(_I64)]),
 }

@@ -1,0 +1,365 @@
+"""GEMM comparison driver: the reference's P3.5 driver shape with the B200 kernel as candidate.
+
+Same command-line contract as src/gemm/gemm_comparison.py (build_arg_parser,
+:3280-3332): --warmup-iterations [1..100] (default 5), --iterations [1..100]
+(default 20), --self-test (GPU-free), CSV on stdout only after every row
+passed its correctness check, diagnostics on stderr, exit 0 / 1 (failure) /
+2 (usage). Per shape: operands built once outside every timer, output
+NaN-prefilled before each candidate, correctness before timing, CUDA-event
+steady state over `iterations` launches (gemm_comparison.py:3055-3074).
+
+Additions for B200: --shapes picks the shape set (the reference's five frozen
+shapes by default; also the benchmark configs c1/c4/c5), --operands picks the
+reference's integer operands (seed 1111, exact fp32 results) or the configs'
+seeded distributions, --out-dtype f32 (reference contract) or bf16, and the
+candidates are the B200 persistent 1-CTA and 2-CTA kernels plus cuBLAS
+(torch.matmul) as a context baseline.
+"""
+from __future__ import annotations
+
+import argparse
+import io
+import math
+import sys
+
+SCHEMA_VERSION = "b200.p35.1"
+EXPERIMENT = "gemm_comparison"
+UNIT = "b200_gemm"
+DEFAULT_WARMUP_ITERATIONS = 5
+DEFAULT_ITERATIONS = 20
+MIN_ITERATIONS = 1
+MAX_ITERATIONS = 100
+
+SHAPE_SETS = {
+    "frozen": ((4096, 4096, 4096), (8192, 8192, 8192), (16384, 512, 4096), (32768, 512, 4096),
+               (512, 16384, 4096)),
+    "c1": ((512, 512, 512),),
+    "c4": ((4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384)),
+    "c5": ((8192, 4096, 4096), (8192, 14336, 4096), (8192, 4096, 14336), (8192, 128256, 4096)),
+}
+
+CANDIDATES = (
+    {"method": "b200", "variant": "persistent_1cta", "mode": "1cta", "mma_tiler": (128, 256),
+     "cluster": (1, 1), "use_2cta_instrs": False},
+    {"method": "b200", "variant": "persistent_2cta", "mode": "2cta", "mma_tiler": (256, 256),
+     "cluster": (2, 1), "use_2cta_instrs": True},
+    {"method": "cublas", "variant": "torch_matmul", "mode": None, "mma_tiler": None,
+     "cluster": None, "use_2cta_instrs": None},
+)
+BASELINE_VARIANT = "torch_matmul"
+
+CSV_FIELDS = (
+    "schema_version", "experiment", "unit", "shape_index", "shape_id", "candidate_index",
+    "method", "variant", "m", "n", "k", "l", "ab_dtype", "acc_dtype", "c_dtype", "a_major",
+    "b_major", "c_major", "mma_tiler_m", "mma_tiler_n", "cluster_m", "cluster_n",
+    "use_2cta_instrs", "use_tma_store", "stages", "grid_ctas", "waves_count", "seed",
+    "operands", "reference", "atol", "rtol", "correctness", "max_abs_error", "max_rel_error",
+    "kernel_time_ms", "warmup_iterations", "iterations", "flop_count", "tflops",
+    "throughput_ratio_vs_cublaslt", "gap_to_cublaslt_pct", "rank_within_shape",
+    "roofline_fraction", "peak_tflops", "n_gpus", "gpu_name", "compute_capability",
+    "publishable",
+)
+
+
+class UsageError(Exception):
+    pass
+
+
+def bounded_int(lo, hi):
+    def parse(text):
+        try:
+            v = int(text, 10)
+        except ValueError as exc:
+            raise argparse.ArgumentTypeError(f"{text!r} is not an integer") from exc
+        if v < lo or v > hi:
+            raise argparse.ArgumentTypeError(f"{v} is outside [{lo}, {hi}]")
+        return v
+    return parse
+
+
+def parse_shape(text: str):
+    parts = text.lower().split("x")
+    if len(parts) != 3:
+        raise argparse.ArgumentTypeError(f"shape {text!r} must be MxNxK")
+    try:
+        m, n, k = (int(p) for p in parts)
+    except ValueError as exc:
+        raise argparse.ArgumentTypeError(f"shape {text!r} must be MxNxK integers") from exc
+    if min(m, n, k) <= 0:
+        raise argparse.ArgumentTypeError(f"shape {text!r} must be positive")
+    return (m, n, k)
+
+
+def build_arg_parser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(prog="gemm_comparison",
+                                description=__doc__.split("\n\n")[0])
+    p.add_argument("--warmup-iterations", type=bounded_int(MIN_ITERATIONS, MAX_ITERATIONS),
+                   default=DEFAULT_WARMUP_ITERATIONS, metavar="N")
+    p.add_argument("--iterations", type=bounded_int(MIN_ITERATIONS, MAX_ITERATIONS),
+                   default=DEFAULT_ITERATIONS, metavar="N")
+    p.add_argument("--self-test", action="store_true",
+                   help="run the GPU-free self-test and exit (no CUDA, nothing on stdout)")
+    p.add_argument("--shapes", choices=sorted(SHAPE_SETS), default="frozen")
+    p.add_argument("--shape", type=parse_shape, action="append", default=None,
+                   help="explicit MxNxK (repeatable); overrides --shapes")
+    p.add_argument("--operands", choices=("ref-compat", "config"), default="ref-compat")
+    p.add_argument("--out-dtype", choices=("f32", "bf16"), default="f32")
+    p.add_argument("--candidates", default="persistent_1cta,persistent_2cta,torch_matmul")
+    p.add_argument("--peak-tflops", type=float, default=None,
+                   help="roofline denominator (default: MEASURED_PEAKS.json bf16_tflops)")
+    return p
+
+
+def select_candidates(spec: str):
+    names = [s.strip() for s in spec.split(",") if s.strip()]
+    known = {c["variant"]: c for c in CANDIDATES}
+    bad = [n for n in names if n not in known]
+    if bad or not names:
+        raise UsageError(f"unknown candidate(s) {bad}; choose from {sorted(known)}")
+    return [known[n] for n in names]
+
+
+def comparison_fields(flop: int, times_ms, variants):
+    """tflops, ratio/gap vs the cuBLAS baseline (if present) and rank, per candidate."""
+    from ..formulas import compute_ratio_and_gap, compute_tflops
+    tflops = [compute_tflops(flop, t) for t in times_ms]
+    base = tflops[variants.index(BASELINE_VARIANT)] if BASELINE_VARIANT in variants else None
+    order = sorted(range(len(times_ms)), key=lambda i: (times_ms[i], i))
+    rank = [0] * len(times_ms)
+    for pos, i in enumerate(order):
+        rank[i] = pos + 1
+    out = []
+    for i, tf in enumerate(tflops):
+        if base is None:
+            ratio, gap = None, None
+        elif variants[i] == BASELINE_VARIANT:
+            ratio, gap = 1.0, 0.0
+        else:
+            ratio, gap = compute_ratio_and_gap(tf, base)
+        out.append({"tflops": tf, "throughput_ratio_vs_cublaslt": ratio,
+                    "gap_to_cublaslt_pct": gap, "rank_within_shape": rank[i]})
+    return out
+
+
+def format_csv(rows) -> str:
+    buf = io.StringIO()
+    buf.write(",".join(CSV_FIELDS) + "\n")
+    for r in rows:
+        vals = []
+        for f in CSV_FIELDS:
+            v = r.get(f)
+            if v is None:
+                vals.append("")
+            elif isinstance(v, bool):
+                vals.append("true" if v else "false")
+            elif isinstance(v, float):
+                vals.append(repr(v) if math.isfinite(v) else "nan")
+            else:
+                s = str(v)
+                vals.append('"' + s.replace('"', '""') + '"' if ("," in s or '"' in s) else s)
+        buf.write(",".join(vals) + "\n")
+    return buf.getvalue()
+
+
+def run_self_test() -> int:
+    """GPU-free checks of the argument contract, formulas and CSV emitter."""
+    from .. import formulas
+    failures = []
+
+    def expect(cond, what):
+        if not cond:
+            failures.append(what)
+
+    parser = build_arg_parser()
+    saved, sys.stderr = sys.stderr, io.StringIO()  # argparse prints usage on rejection
+    try:
+        _expect_rejections(parser, expect)
+    finally:
+        sys.stderr = saved
+    ns = parser.parse_args([])
+    expect(ns.iterations == 20 and ns.warmup_iterations == 5, "defaults")
+    _rest_of_self_test(expect, formulas)
+    for f in failures:
+        print(f"gemm_comparison: SELF_TEST FAIL {f}", file=sys.stderr)
+    print(f"gemm_comparison: SELF_TEST_RESULT={'PASS' if not failures else 'FAIL'}",
+          file=sys.stderr)
+    return 0 if not failures else 1
+
+
+def _expect_rejections(parser, expect):
+    for bad in (["--iterations", "0"], ["--iterations", "101"], ["--warmup-iterations", "x"],
+                ["--shape", "1x2"], ["--shape", "0x1x1"]):
+        try:
+            parser.parse_args(bad)
+            expect(False, f"accepted {bad}")
+        except SystemExit:
+            pass
+
+
+def _rest_of_self_test(expect, formulas):
+    expect(formulas.compute_flop_count(8192, 8192, 8192) == 1099511627776, "flop 8192^3")
+    expect(abs(formulas.compute_tflops(1099511627776, 0.519) - 2118.5195140192677) < 1e-9,
+           "tflops")
+    rows = comparison_fields(2 * 512 ** 3, [0.010, 0.008, 0.020],
+                             ["persistent_1cta", "persistent_2cta", "torch_matmul"])
+    expect([r["rank_within_shape"] for r in rows] == [2, 1, 3], "ranks")
+    expect(rows[2]["throughput_ratio_vs_cublaslt"] == 1.0 and rows[2]["gap_to_cublaslt_pct"] == 0.0,
+           "baseline ratio")
+    expect(abs(rows[1]["throughput_ratio_vs_cublaslt"] - 2.5) < 1e-12, "ratio")
+    expect(abs(rows[1]["gap_to_cublaslt_pct"] + 150.0) < 1e-9, "gap")
+    text = format_csv([{"shape_id": "1x2", "method": "a,b", "tflops": 1.5, "publishable": False}])
+    lines = text.strip().split("\n")
+    expect(len(lines) == 2 and lines[0].split(",") == list(CSV_FIELDS), "csv header")
+    expect('"a,b"' in lines[1] and "false" in lines[1], "csv quoting")
+    try:
+        select_candidates("nope")
+        expect(False, "accepted unknown candidate")
+    except UsageError:
+        pass
+
+
+def _peak(args):
+    if args.peak_tflops:
+        return args.peak_tflops
+    import json
+    from pathlib import Path
+    p = Path(__file__).resolve().parents[3] / "MEASURED_PEAKS.json"
+    if p.is_file():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
+
+
+def execute_measurement(args) -> str:
+    import torch
+
+    from .. import check, operands
+    from ..gemm import GemmPlan
+
+    if not torch.cuda.is_available():
+        raise RuntimeError("no CUDA device is visible")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    props = torch.cuda.get_device_properties(dev)
+    shapes = args.shape if args.shape else SHAPE_SETS[args.shapes]
+    cands = select_candidates(args.candidates)
+    out_dtype = torch.float32 if args.out_dtype == "f32" else torch.bfloat16
+    peak = _peak(args)
+    rows = []
+    stream = torch.cuda.current_stream(dev)
+    for si, (m, n, k) in enumerate(shapes):
+        if args.operands == "ref-compat":
+            if operands.ref_compat_available():
+                a_h, b_h = operands.ref_compat_operands(m, n, k)
+                seed, opname = operands.REF_SEED, "cutlass.torch.matrix(seed 1111)"
+            else:
+                a_h, b_h = operands.integer_operands(m, n, k)
+                seed, opname = operands.REF_SEED, "integer{-2..1}(seed 1111)"
+        else:
+            a_h, b_h = operands.uniform_operands(m, n, k, seed=0) if (m, n, k) == (512, 512, 512) \
+                else operands.normal_operands(m, n, k, seed=1, std_a=0.1, std_b=0.1)
+            seed, opname = (0 if (m, n, k) == (512, 512, 512) else 1), "config"
+        a = a_h.to(dev)
+        b = b_h.to(dev)
+        # The reference's oracle: IEEE fp32 matmul on the GPU (gemm_comparison.py:2705-2722).
+        torch.backends.cuda.matmul.fp32_precision = "ieee"
+        reference = torch.einsum("mk,nk->mn", a.float(), b.float())
+        out = torch.empty((m, n), dtype=out_dtype, device=dev)
+        times, metas = [], []
+        for cand in cands:
+            out.fill_(float("nan"))
+            torch.cuda.synchronize()
+            if cand["method"] == "b200":
+                plan = GemmPlan(a, b, out, mode=cand["mode"], stream=stream)
+                launch = plan.execute
+                meta = plan.info
+            else:
+                plan = None
+
+                def launch(o=out):
+                    torch.matmul(a, b.T, out=o) if o.dtype == torch.bfloat16 else \
+                        torch.matmul(a.float(), b.float().T, out=o)
+                meta = {}
+            launch()
+            if plan is not None:
+                plan.synchronize()
+            torch.cuda.synchronize()
+            label = f"{m}x{n}x{k}/{cand['variant']}"
+            if out_dtype == torch.float32:
+                max_abs, max_rel = check.validate_result(label, reference, out)
+            else:
+                stats = check.bf16_tolerance_check(label, reference, out, k,
+                                                   float(a_h.float().abs().max()),
+                                                   float(b_h.float().abs().max()))
+                max_abs, max_rel = stats["max_abs_error"], stats["rel_fro"]
+            for _ in range(args.warmup_iterations):
+                launch()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.iterations):
+                launch()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if plan is not None:
+                plan.synchronize()
+                plan.destroy()
+            times.append(e0.elapsed_time(e1) / args.iterations)
+            metas.append((cand, meta, max_abs, max_rel))
+        flop = 2 * m * n * k
+        comp = comparison_fields(flop, times, [c["variant"] for c in cands])
+        for ci, ((cand, meta, max_abs, max_rel), t, cf) in enumerate(zip(metas, times, comp)):
+            rows.append({
+                "schema_version": SCHEMA_VERSION, "experiment": EXPERIMENT, "unit": UNIT,
+                "shape_index": si, "shape_id": f"{m}x{n}x{k}x1", "candidate_index": ci,
+                "method": cand["method"], "variant": cand["variant"], "m": m, "n": n, "k": k,
+                "l": 1, "ab_dtype": "BFloat16", "acc_dtype": "Float32",
+                "c_dtype": "Float32" if out_dtype == torch.float32 else "BFloat16",
+                "a_major": "k", "b_major": "k", "c_major": "n",
+                "mma_tiler_m": cand["mma_tiler"][0] if cand["mma_tiler"] else None,
+                "mma_tiler_n": cand["mma_tiler"][1] if cand["mma_tiler"] else None,
+                "cluster_m": cand["cluster"][0] if cand["cluster"] else None,
+                "cluster_n": cand["cluster"][1] if cand["cluster"] else None,
+                "use_2cta_instrs": cand["use_2cta_instrs"],
+                "use_tma_store": cand["method"] == "b200",
+                "stages": meta.get("stages"), "grid_ctas": meta.get("grid_ctas"),
+                "waves_count": meta.get("waves"), "seed": seed, "operands": opname,
+                "reference": "torch_fp32_ieee_einsum", "atol": check.REF_ATOL,
+                "rtol": check.REF_RTOL, "correctness": "PASS", "max_abs_error": max_abs,
+                "max_rel_error": max_rel, "kernel_time_ms": t,
+                "warmup_iterations": args.warmup_iterations, "iterations": args.iterations,
+                "flop_count": flop, "roofline_fraction": cf["tflops"] / peak,
+                "peak_tflops": peak, "n_gpus": 1, "gpu_name": props.name,
+                "compute_capability": f"{props.major}.{props.minor}", "publishable": False,
+                **cf,
+            })
+            print(f"gemm_comparison: {m}x{n}x{k} {cand['variant']}: {t:.4f} ms "
+                  f"{cf['tflops']:.1f} TFLOP/s max_abs={max_abs:.3g}", file=sys.stderr)
+        del a, b, out, reference
+        torch.cuda.empty_cache()
+    return format_csv(rows)
+
+
+def main(argv=None) -> int:
+    parser = build_arg_parser()
+    try:
+        args = parser.parse_args(argv)
+    except SystemExit as exc:
+        return 2 if exc.code else 0
+    if args.self_test:
+        return run_self_test()
+    try:
+        select_candidates(args.candidates)
+        text = execute_measurement(args)
+    except UsageError as exc:
+        print(f"gemm_comparison: ERROR: {exc}", file=sys.stderr)
+        return 2
+    except Exception as exc:  # every failure: no CSV, exit 1
+        print(f"gemm_comparison: ERROR: {type(exc).__name__}: {exc}", file=sys.stderr)
+        return 1
+    sys.stdout.write(text)
+    sys.stdout.flush()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -50,6 +50,7 @@ enum {
     B200_DEV_TIMEOUT_EPILOGUE = 0x104, /* epilogue waited too long for an accumulator */
     B200_DEV_TIMEOUT_STREAM = 0x105,   /* memory-path streamer waited too long for a stage */
     B200_DEV_TIMEOUT_UMMA = 0x106,     /* UMMA probe waited too long for its commit */
+    B200_DEV_TIMEOUT_SELFTEST = 0x107, /* b200_selftest_bounded_wait ran out, as designed */
     B200_DEV_BAD_LAUNCH = 0x1FF        /* launch geometry differs from the kernel's contract */
 };
 
@@ -279,6 +280,17 @@ int b200_umma_probe(const B200UmmaConfig* cfg, const void* a, const void* b, flo
  * reference (it has no multi-GPU path). */
 int b200_shard_range(int64_t n, int64_t world, int64_t rank, int64_t granule, int64_t* n_begin,
                      int64_t* n_end);
+
+/* ------------------------------------------------------------------------ */
+/* Failure detection                                                         */
+/* ------------------------------------------------------------------------ */
+
+/* Launches one kernel that waits on an mbarrier nothing arrives on, with a
+ * budget of timeout_ns; the wait gives up, writes B200_DEV_TIMEOUT_SELFTEST to
+ * *status (device int, caller-zeroed) and the kernel returns normally. Tests
+ * the bounded-wait machinery every kernel here relies on instead of the
+ * reference's unbounded spins (src/memory/tma.cu:404-408). */
+int b200_selftest_bounded_wait(unsigned long long timeout_ns, int* status, void* stream);
 
 #ifdef __cplusplus
 }

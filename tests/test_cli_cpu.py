@@ -1,0 +1,59 @@
+"""Command-line contracts of the drivers without a GPU (exit codes, self-test)."""
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+ENV_PATH = str(REPO / "gb300-gemm-anatomy_b200")
+
+
+def run(mod, *args):
+    import os
+    env = dict(os.environ, PYTHONPATH=ENV_PATH + os.pathsep + str(REPO), CUDA_VISIBLE_DEVICES="")
+    return subprocess.run([sys.executable, "-m", mod, *args], capture_output=True, text=True,
+                          env=env, timeout=120)
+
+
+def test_gemm_comparison_self_test():
+    r = run("b200gemm.cli.gemm_comparison", "--self-test")
+    assert r.returncode == 0 and "SELF_TEST_RESULT=PASS" in r.stderr and r.stdout == ""
+
+
+@pytest.mark.parametrize("args", [["--iterations", "0"], ["--iterations", "101"],
+                                  ["--warmup-iterations", "abc"], ["--shape", "8x8"],
+                                  ["--candidates", "nope"]])
+def test_gemm_comparison_usage_errors(args):
+    r = run("b200gemm.cli.gemm_comparison", *args)
+    assert r.returncode == 2 and r.stdout == ""
+
+
+@pytest.mark.parametrize("args", [["--stages", "3"], ["--stages", "4"],
+                                  ["--stages", "4", "--bytes-in-flight-kib", "64"],
+                                  ["--bytes-in-flight-kib", "48"]])
+def test_memory_paths_usage_errors(args):
+    r = run("b200gemm.cli.memory_paths", *args)
+    assert r.returncode == 2 and r.stdout == ""
+
+
+def test_memory_paths_needs_gpu_and_fails_cleanly():
+    r = run("b200gemm.cli.memory_paths", "--stages", "4", "--bytes-in-flight-kib", "64",
+            "--run-kind", "smoke")
+    assert r.returncode == 1 and r.stdout == "" and "ERROR" in r.stderr
+
+
+@pytest.mark.parametrize("args", [["--n", "96"], ["--depth", "5"], ["--iterations", "0"]])
+def test_umma_usage_errors(args):
+    r = run("b200gemm.cli.umma", *args)
+    assert r.returncode == 2 and r.stdout == ""
+
+
+def test_memory_paths_grids():
+    sys.path.insert(0, ENV_PATH)
+    from b200gemm.cli import memory_paths as mp
+    ref = mp.reference_grid()
+    assert len(ref) == 18 and {g[1] for g in ref} == {2, 4, 8}
+    assert sorted({g[2] * g[1] // 1024 for g in ref}) == [16, 32, 64]
+    base = mp.baseline_grid()
+    assert {g[3] for g in base} == {1, 2, 4} and {g[2] for g in base} == {16384}
