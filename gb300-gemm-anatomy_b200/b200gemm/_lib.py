@@ -123,6 +123,7 @@ SIGNATURES = {
     "b200_gemm_supported": (_INT, [_I64, _I64, _I64, _I64, _INT, _INT]),
     "b200_gemm": (_INT, [_I64, _I64, _I64, _P, _P, _P, _I64, _INT, _INT, _P]),
     "b200_gemm_plan_launches": (_I64, [_P]),
+    "b200_gemm_plan_set_trace": (_INT, [_P, _P, _I64]),
     "b200_gemm_noalloc": (_INT, [_I64, _I64, _I64, _P, _P, _P, _I64, _INT, _INT, _P]),
     "b200_fill_pattern": (_INT, [_P, _I64, _P]),
     "b200_stream_plan_create": (_INT, [ctypes.POINTER(StreamConfig), _P, _I64, _INT,

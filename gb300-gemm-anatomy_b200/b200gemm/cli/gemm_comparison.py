@@ -45,8 +45,13 @@ CANDIDATES = (
      "cluster": (2, 1), "use_2cta_instrs": True},
     {"method": "cublas", "variant": "torch_matmul", "mode": None, "mma_tiler": None,
      "cluster": None, "use_2cta_instrs": None},
+    # The reference's own cuBLASLt bridge (cublaslt_bridge_p35.cu), built unmodified by
+    # baseline/build_ref_bridge.sh; context baseline for its five frozen shapes, fp32 D.
+    {"method": "cublaslt", "variant": "heuristic_first_supported", "mode": None,
+     "mma_tiler": None, "cluster": None, "use_2cta_instrs": None},
 )
-BASELINE_VARIANT = "torch_matmul"
+REF_BRIDGE = "baseline/_ref/libcublaslt_bridge_p35.so"
+BASELINE_VARIANTS = ("heuristic_first_supported", "torch_matmul")
 
 CSV_FIELDS = (
     "schema_version", "experiment", "unit", "shape_index", "shape_id", "candidate_index",
@@ -104,7 +109,9 @@ def build_arg_parser() -> argparse.ArgumentParser:
                    help="explicit MxNxK (repeatable); overrides --shapes")
     p.add_argument("--operands", choices=("ref-compat", "config"), default="ref-compat")
     p.add_argument("--out-dtype", choices=("f32", "bf16"), default="f32")
-    p.add_argument("--candidates", default="persistent_1cta,persistent_2cta,torch_matmul")
+    p.add_argument("--candidates", default="persistent_1cta,persistent_2cta,torch_matmul",
+                   help="comma list of persistent_1cta, persistent_2cta, torch_matmul, "
+                        "heuristic_first_supported (the reference's cuBLASLt bridge)")
     p.add_argument("--peak-tflops", type=float, default=None,
                    help="roofline denominator (default: MEASURED_PEAKS.json bf16_tflops)")
     return p
@@ -123,7 +130,8 @@ def comparison_fields(flop: int, times_ms, variants):
     """tflops, ratio/gap vs the cuBLAS baseline (if present) and rank, per candidate."""
     from ..formulas import compute_ratio_and_gap, compute_tflops
     tflops = [compute_tflops(flop, t) for t in times_ms]
-    base = tflops[variants.index(BASELINE_VARIANT)] if BASELINE_VARIANT in variants else None
+    base_name = next((v for v in BASELINE_VARIANTS if v in variants), None)
+    base = tflops[variants.index(base_name)] if base_name else None
     order = sorted(range(len(times_ms)), key=lambda i: (times_ms[i], i))
     rank = [0] * len(times_ms)
     for pos, i in enumerate(order):
@@ -132,7 +140,7 @@ def comparison_fields(flop: int, times_ms, variants):
     for i, tf in enumerate(tflops):
         if base is None:
             ratio, gap = None, None
-        elif variants[i] == BASELINE_VARIANT:
+        elif variants[i] == base_name:
             ratio, gap = 1.0, 0.0
         else:
             ratio, gap = compute_ratio_and_gap(tf, base)
@@ -229,6 +237,52 @@ def _peak(args):
     return 1590.0
 
 
+class _RefBridgePlan:
+    """One plan of the reference's unmodified cuBLASLt bridge (p35_* C ABI)."""
+
+    def __init__(self, m, n, k, a, b, out, stream):
+        import ctypes
+        from pathlib import Path
+        path = Path(__file__).resolve().parents[3] / REF_BRIDGE
+        if not path.is_file():
+            raise UsageError(f"{path} is missing; build it with baseline/build_ref_bridge.sh")
+        lib = ctypes.CDLL(str(path))
+        lib.p35_plan_info_size.restype = ctypes.c_size_t
+        lib.p35_last_error.restype = ctypes.c_char_p
+        lib.p35_plan_create.restype = ctypes.c_int
+        lib.p35_plan_create.argtypes = [ctypes.c_int64] * 3 + [ctypes.c_void_p] * 5 + [
+            ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
+        for name in ("p35_plan_execute", "p35_stream_synchronize", "p35_plan_destroy"):
+            getattr(lib, name).restype = ctypes.c_int
+            getattr(lib, name).argtypes = [ctypes.c_void_p]
+        self.info = ctypes.create_string_buffer(int(lib.p35_plan_info_size()))
+        self.plan = ctypes.c_void_p()
+        rc = lib.p35_plan_create(m, n, k, a.data_ptr(), b.data_ptr(), out.data_ptr(),
+                                 out.data_ptr(), int(stream.cuda_stream), ctypes.byref(self.plan),
+                                 self.info)
+        if rc != 0:
+            raise UsageError(f"reference bridge refused {m}x{n}x{k}: {lib.p35_last_error()!r}")
+        self.lib = lib
+
+    def execute(self):
+        if self.lib.p35_plan_execute(self.plan) != 0:
+            raise RuntimeError(f"p35_plan_execute failed: {self.lib.p35_last_error()!r}")
+
+    def synchronize(self):
+        if self.lib.p35_stream_synchronize(self.plan) != 0:
+            raise RuntimeError(f"p35_stream_synchronize failed: {self.lib.p35_last_error()!r}")
+
+    def destroy(self):
+        if self.plan:
+            self.lib.p35_plan_destroy(self.plan)
+            self.plan = ctypes_null()
+
+
+def ctypes_null():
+    import ctypes
+    return ctypes.c_void_p()
+
+
 def execute_measurement(args) -> str:
     import torch
 
@@ -272,12 +326,21 @@ def execute_measurement(args) -> str:
                 plan = GemmPlan(a, b, out, mode=cand["mode"], stream=stream)
                 launch = plan.execute
                 meta = plan.info
+            elif cand["method"] == "cublaslt":
+                if out_dtype != torch.float32:
+                    raise UsageError("the reference cuBLASLt bridge writes fp32 D only")
+                plan = _RefBridgePlan(m, n, k, a, b, out, stream)
+                launch = plan.execute
+                meta = {}
             else:
                 plan = None
 
                 def launch(o=out):
-                    torch.matmul(a, b.T, out=o) if o.dtype == torch.bfloat16 else \
-                        torch.matmul(a.float(), b.float().T, out=o)
+                    # bf16 x bf16 with fp32 accumulation; fp32 D via aten::mm.dtype.
+                    if o.dtype == torch.bfloat16:
+                        torch.matmul(a, b.T, out=o)
+                    else:
+                        torch.mm(a, b.T, out_dtype=torch.float32, out=o)
                 meta = {}
             launch()
             if plan is not None:

@@ -116,11 +116,19 @@ def make_buffer(nbytes, fill, dev):
     return buf
 
 
+_HOST_CHECKSUMS = {}
+
+
 def host_checksum(buf):
+    """XOR/sum of the buffer's 32-bit words, computed on the host (cached per buffer)."""
     import numpy as np
+    key = (buf.data_ptr(), buf.numel() * buf.element_size())
+    if key in _HOST_CHECKSUMS:
+        return _HOST_CHECKSUMS[key]
     words = buf.view(__import__("torch").int32).cpu().numpy().view(np.uint32)
     x = int(np.bitwise_xor.reduce(words)) if words.size else 0
     s = int(words.sum(dtype=np.uint64)) & ((1 << 64) - 1)
+    _HOST_CHECKSUMS[key] = (x, s)
     return x, s
 
 

@@ -80,6 +80,17 @@ class GemmPlan:
     def launches_per_execute(self) -> int:
         return int(self._lib.b200_gemm_plan_launches(self._plan))
 
+    TRACE_SLOTS = 64
+
+    def enable_trace(self) -> torch.Tensor:
+        """Allocate and attach a per-CTA timeline buffer (see b200_gemm_plan_set_trace)."""
+        buf = torch.zeros((max(self.info["grid_ctas"], 1), self.TRACE_SLOTS), dtype=torch.int64,
+                          device=self.a.device)
+        _lib.check(self._lib.b200_gemm_plan_set_trace(self._plan, buf.data_ptr(), self.TRACE_SLOTS),
+                   "b200_gemm_plan_set_trace", self._lib)
+        self._trace = buf
+        return buf
+
     def execute(self, stream=None) -> None:
         if self._plan is None:
             raise BridgeError("the plan was destroyed")

@@ -27,6 +27,7 @@
 // and signals the leader's full barrier; the leader's commits are sent to each
 // CTA's barrier separately (two unicast commits, no multicast anywhere).
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -65,21 +66,38 @@ struct GemmParams {
     int m, n, k;
     int num_m_blocks, num_n_blocks, num_k_blocks;
     int num_tiles;
-    int group_m;
+    int group_m;     // blocks per raster group along the grouped dimension
+    int raster_n;    // 0: groups of m-blocks walk all n-blocks; 1: groups of n-blocks walk all m-blocks
     int* status;
     unsigned long long timeout_ns;
+    // Optional timeline (nullptr = off): per CTA kTraceSlots %globaltimer stamps.
+    unsigned long long* trace;
 };
+
+// Trace slots per CTA: 0 entry, 1 setup done, 2 producer done, 3 MMA done,
+// 4 epilogue done, 5 exit, 6.. the epilogue's "accumulator ready" time of each
+// tile this CTA processed (up to kTraceSlots - 6 tiles).
+constexpr int kTraceSlots = 64;
+
+__device__ __forceinline__ void trace_stamp(const GemmParams& p, int slot) {
+    if (p.trace != nullptr && slot < kTraceSlots)
+        p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = globaltimer_ns();
+}
 
 // Linear tile id -> (m block, n block): M-grouped raster so that the tiles in
 // flight at one time share A rows and B rows in L2.
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mb, int& nb) {
-    const int per_group = p.group_m * p.num_n_blocks;
+    const int major = p.raster_n ? p.num_n_blocks : p.num_m_blocks;  // grouped dimension
+    const int minor = p.raster_n ? p.num_m_blocks : p.num_n_blocks;
+    const int per_group = p.group_m * minor;
     const int g = t / per_group;
-    const int first_m = g * p.group_m;
-    const int gm = min(p.group_m, p.num_m_blocks - first_m);
+    const int first = g * p.group_m;
+    const int gsize = min(p.group_m, major - first);
     const int r = t - g * per_group;
-    mb = first_m + r % gm;
-    nb = r / gm;
+    const int a = first + r % gsize;
+    const int b = r / gsize;
+    mb = p.raster_n ? b : a;
+    nb = p.raster_n ? a : b;
 }
 
 template <int kCtaGroup, bool kOutF32>
@@ -99,6 +117,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         return;
     }
 
+    if (threadIdx.x == 0) trace_stamp(p, 0);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -139,6 +158,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
     if constexpr (kPair) cluster_sync(); else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+    if (threadIdx.x == 0) trace_stamp(p, 1);
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -172,6 +192,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
                 }
             }
+            trace_stamp(p, 2);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -222,6 +243,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1;
             }
+            trace_stamp(p, 3);
         }
         __syncwarp();
     } else {
@@ -229,13 +251,15 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const uint32_t stage_buf0 = sbase + C::kEpiOffset + q * 2 * kEpiBufBytes;
         uint32_t acc = 0, acc_phase = 0, buf = 0;
-        for (int t = cluster_id; t < p.num_tiles; t += num_clusters) {
+        int local_tile = 0;
+        for (int t = cluster_id; t < p.num_tiles; t += num_clusters, ++local_tile) {
             int mb, nb;
             tile_coords(t, p, mb, nb);
             if (!mbar_wait<kPair>(tfull0 + 8 * acc, acc_phase, p.status, p.timeout_ns,
                                   B200_DEV_TIMEOUT_EPILOGUE)) {
                 break;
             }
+            if (warp == 2 && lane == 0) trace_stamp(p, 6 + local_tile);
             tc_fence_after();
             const int row0 = mb * C::kTileM + static_cast<int>(rank) * kRowsPerCta + q * 32;
             const int col0 = nb * kBN;
@@ -289,6 +313,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         }
         if (lane == 0) bulk_wait_group<0>();
         __syncwarp();
+        if (warp == 2 && lane == 0) trace_stamp(p, 4);
     }
 
     // Teardown: every role is done with TMEM and with the peer's barriers.
@@ -298,6 +323,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         tc_fence_after();
         tmem_dealloc<kCtaGroup>(tmem_base, kTmemCols);
     }
+    if (threadIdx.x == 0) trace_stamp(p, 5);
 }
 
 // ---------------------------------------------------------------------------
@@ -379,6 +405,21 @@ static int check_shape(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dty
     return B200_OK;
 }
 
+// Raster of the persistent tile walk. Overridable for tuning with
+// B200_GEMM_GROUP (blocks per group, >= 1) and B200_GEMM_RASTER ("m" or "n").
+static void raster_for(const GemmParams& p, int* group, int* raster_n) {
+    // 8 m-blocks per group: the 74-148 tiles in flight then span ~8 x 9 blocks,
+    // which measured the least DRAM traffic at 8192^3 (1.11 GB vs 1.26 GB at 16).
+    *group = 8;
+    *raster_n = 0;
+    if (const char* g = std::getenv("B200_GEMM_GROUP")) {
+        const int v = std::atoi(g);
+        if (v >= 1 && v <= 4096) *group = v;
+    }
+    if (const char* r = std::getenv("B200_GEMM_RASTER")) *raster_n = (r[0] == 'n' || r[0] == 'N');
+    (void)p;
+}
+
 static int resolve_mode(int mode, int64_t m) {
     if (mode != B200_MODE_AUTO) return mode;
     return m >= 256 ? B200_MODE_2CTA : B200_MODE_1CTA;
@@ -447,7 +488,7 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
     p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
     p.num_k_blocks = static_cast<int>((k + kBK - 1) / kBK);
     p.num_tiles = p.num_m_blocks * p.num_n_blocks;
-    p.group_m = 16;
+    raster_for(p, &p.group_m, &p.raster_n);
     p.timeout_ns = wait_timeout_ns();
 
     cudaError_t err = cudaMalloc(&plan->d_status, sizeof(int));
@@ -667,6 +708,21 @@ int b200_gemm_plan_destroy(B200Plan* plan) {
     B200_ABI_GUARD_END
 }
 
+int b200_gemm_plan_set_trace(B200Plan* plan, unsigned long long* trace, int64_t slots_per_cta) {
+    b200::clear_error();
+    if (plan == nullptr) {
+        b200::set_error("plan is NULL");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (trace != nullptr && slots_per_cta != b200::kTraceSlots) {
+        b200::set_error("the trace buffer must hold %d slots per CTA (grid_ctas x %d uint64)",
+                        b200::kTraceSlots, b200::kTraceSlots);
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    plan->params.trace = trace;
+    return B200_OK;
+}
+
 int64_t b200_gemm_plan_launches(const B200Plan* plan) {
     if (plan == nullptr || plan->empty_problem) return 0;
     return 1;
@@ -760,7 +816,7 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
     p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
     p.num_k_blocks = static_cast<int>((k + kBK - 1) / kBK);
     p.num_tiles = p.num_m_blocks * p.num_n_blocks;
-    p.group_m = 16;
+    raster_for(p, &p.group_m, &p.raster_n);
     p.timeout_ns = wait_timeout_ns();
     p.status = status;
     if (plan->empty_problem) return B200_OK;

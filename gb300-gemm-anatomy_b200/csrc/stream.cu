@@ -85,6 +85,27 @@ __device__ __forceinline__ void tile_range(const StreamParams& p, int64_t& begin
     count = end - begin;
 }
 
+// Walks a CTA's tiles pass after pass, each pass rotated by one more tile
+// (the reference's rotation, ldgsts.cu:351-356), with one modulo per pass
+// instead of 64-bit divisions per step.
+struct TileWalk {
+    int64_t begin, count, rotation;
+    int64_t i = 0, pass = 0, j = 0;
+    __device__ TileWalk(int64_t b, int64_t c, int64_t rot) : begin(b), count(c), rotation(rot) {
+        j = count > 0 ? rot % count : 0;
+    }
+    __device__ __forceinline__ int64_t tile() const { return begin + j; }
+    __device__ __forceinline__ void next() {
+        ++i;
+        if (++j == count) j = 0;
+        if (i == count) {
+            i = 0;
+            ++pass;
+            j = (rotation + pass) % count;
+        }
+    }
+};
+
 // Per-thread consumption state.
 struct Consumer {
     unsigned long long mismatches = 0;
@@ -144,23 +165,15 @@ ldgsts_stream_kernel(const StreamParams p) {
     const uint32_t sbase = smem_u32(smem);
     const int64_t total_steps = ntiles * p.passes;
 
-    auto tile_of = [&](int64_t step) -> int64_t {
-        const int64_t pass = step / ntiles;
-        const int64_t i = step - pass * ntiles;
-        const int64_t rot = (p.rotation + pass) % ntiles;
-        int64_t j = i + rot;
-        if (j >= ntiles) j -= ntiles;
-        return tile0 + j;
-    };
+    TileWalk issue_walk(tile0, ntiles, p.rotation), use_walk(tile0, ntiles, p.rotation);
+    const uint32_t stage_bytes = static_cast<uint32_t>(p.stage_bytes);
     auto issue = [&](int64_t step) {
         if (step < total_steps) {
-            const int64_t tile = tile_of(step);
-            const uint8_t* src = p.src + tile * p.stage_bytes;
-            const uint32_t slot = sbase + static_cast<uint32_t>((step % STAGES) * p.stage_bytes);
-            for (int c = 0; c < copies; ++c) {
-                const int v = tid + c * kStreamThreads;
-                cp_async_16(slot + v * 16, src + static_cast<int64_t>(v) * 16);
-            }
+            const uint8_t* src = p.src + issue_walk.tile() * p.stage_bytes + tid * 16;
+            const uint32_t slot = sbase + static_cast<uint32_t>(step % STAGES) * stage_bytes + tid * 16;
+            for (int c = 0; c < copies; ++c)
+                cp_async_16(slot + c * (kStreamThreads * 16), src + c * (kStreamThreads * 16));
+            issue_walk.next();
         }
         cp_async_commit();  // possibly empty group: keeps the group count uniform
     };
@@ -170,7 +183,8 @@ ldgsts_stream_kernel(const StreamParams p) {
         for (int64_t step = 0; step < total_steps; ++step) {
             issue(step + STAGES - 1);
             cp_async_wait<STAGES - 1>();
-            const int64_t tile = tile_of(step);
+            const int64_t tile = use_walk.tile();
+            use_walk.next();
             const uint8_t* slot = smem + (step % STAGES) * p.stage_bytes;
             if (p.mode == B200_STREAM_SINK) {
                 cons.sink ^= *reinterpret_cast<const uint32_t*>(slot + tid * 16);
@@ -217,19 +231,13 @@ tma_stream_kernel(const __grid_constant__ CUtensorMap tmap, const StreamParams p
     }
     __syncthreads();
 
-    auto tile_of = [&](int64_t step) -> int64_t {
-        const int64_t pass = step / ntiles;
-        const int64_t i = step - pass * ntiles;
-        const int64_t rot = (p.rotation + pass) % ntiles;
-        int64_t j = i + rot;
-        if (j >= ntiles) j -= ntiles;
-        return tile0 + j;
-    };
+    TileWalk issue_walk(tile0, ntiles, p.rotation), use_walk(tile0, ntiles, p.rotation);
     const int rows_per_tile = p.box_rows * p.boxes_per_stage;
     auto issue = [&](int64_t step) {
         const int s = static_cast<int>(step % STAGES);
         const uint32_t slot = sbase + static_cast<uint32_t>(s * p.stage_bytes);
-        const int64_t row = tile_of(step) * rows_per_tile;
+        const int64_t row = issue_walk.tile() * rows_per_tile;
+        issue_walk.next();
         mbar_arrive_expect_tx(full0 + 8 * s, static_cast<uint32_t>(p.stage_bytes));
         for (int b = 0; b < p.boxes_per_stage; ++b)
             tma_load_2d(slot + b * p.box_rows * p.row_bytes, &tmap, full0 + 8 * s, 0,
@@ -250,10 +258,11 @@ tma_stream_kernel(const __grid_constant__ CUtensorMap tmap, const StreamParams p
             break;
         }
         const uint8_t* slot = smem + s * p.stage_bytes;
+        const int64_t tile = use_walk.tile();
+        use_walk.next();
         if (p.mode == B200_STREAM_SINK) {
             cons.sink ^= *reinterpret_cast<const uint32_t*>(slot + tid * 16);
         } else {
-            const int64_t tile = tile_of(step);
             const uint64_t vec0 = static_cast<uint64_t>(tile * (p.stage_bytes / 16));
             for (int v = tid; v < vecs; v += kStreamThreads) {
                 const uint4 x = *reinterpret_cast<const uint4*>(slot + v * 16);

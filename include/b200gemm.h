@@ -184,6 +184,14 @@ int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, voi
 int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
                       int64_t ldd, int out_dtype, int mode, void* stream);
 
+/* Timeline tracing (off by default). trace: device buffer of grid_ctas x 64
+ * uint64 (%globaltimer ns) that each later execute fills per CTA: [0] entry,
+ * [1] setup done, [2] producer done, [3] MMA issuer done, [4] epilogue done,
+ * [5] exit, [6+i] accumulator of the CTA's i-th tile ready; unused slots keep
+ * their old contents. NULL turns tracing off. No counterpart in the reference
+ * (its UMMA probe times with %clock64 only, src/compute/umma_1sm.cu:449-475). */
+int b200_gemm_plan_set_trace(B200Plan* plan, unsigned long long* trace, int64_t slots_per_cta);
+
 /* Number of device kernels one execute launches (for launch accounting). */
 int64_t b200_gemm_plan_launches(const B200Plan* plan);
 
