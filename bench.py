@@ -67,7 +67,7 @@ def profile_traffic():
 class ClockSampler:
     """nvidia-smi clock/throttle sampling during the timed region."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -81,7 +81,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
@@ -92,6 +92,18 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def mark(self, which: str):
+        """Wall-clock bounds of the timed region; only samples inside it are kept."""
+        setattr(self, which, time.time())
+
+    @staticmethod
+    def _epoch(stamp: str):
+        import datetime
+        try:
+            return datetime.datetime.strptime(stamp.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
 
     def stop(self):
         if self.proc is None:
@@ -105,9 +117,13 @@ class ClockSampler:
             self.t.join(timeout=2)
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        lo, hi = getattr(self, "t_start", None), getattr(self, "t_end", None)
         for line in self.lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
+                continue
+            ts = self._epoch(f[0])
+            if lo is not None and hi is not None and ts is not None and not (lo <= ts <= hi):
                 continue
             try:
                 sm.append(float(f[1]))
@@ -129,16 +145,24 @@ def cpu_reference_sample(a_cpu, b_cpu, budget_s: float):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    rows = 16
+    # Grow the slab until one run costs a quarter of the budget, then scale to it.
+    rows = 64
+    while True:
+        t0 = time.perf_counter()
+        oracle.reference_einsum(a_cpu[:rows], b_cpu)
+        probe = time.perf_counter() - t0
+        if probe >= budget_s / 4 or rows >= a_cpu.shape[0]:
+            break
+        rows = min(a_cpu.shape[0], rows * 4)
+    want = rows * budget_s / max(probe, 1e-4)
+    reps = max(1, int(want // a_cpu.shape[0])) if want > a_cpu.shape[0] else 1
+    rows = int(max(16, min(a_cpu.shape[0], want)))
     t0 = time.perf_counter()
-    oracle.reference_einsum(a_cpu[:rows], b_cpu)
-    probe = max(time.perf_counter() - t0, 1e-4)
-    rows = int(max(16, min(a_cpu.shape[0], rows * budget_s / probe)))
-    t0 = time.perf_counter()
-    oracle.reference_einsum(a_cpu[:rows], b_cpu)
+    for _ in range(reps):
+        oracle.reference_einsum(a_cpu[:rows], b_cpu)
     dt = time.perf_counter() - t0
-    flop = 2.0 * rows * b_cpu.shape[0] * b_cpu.shape[1]
-    return flop / dt / 1e12, threads, rows, dt
+    flop = 2.0 * rows * b_cpu.shape[0] * b_cpu.shape[1] * reps
+    return flop / dt / 1e12, threads, rows * reps, dt
 
 
 def dist_env():
@@ -159,14 +183,14 @@ def run_reference_arm(args):
     a, b = operands.square_operands(M, seed=1)
     threads = os.cpu_count() or 1
     for _ in range(max(args.warmup, 0)):
-        cpu_reference_sample(a, b, 0.5)
+        cpu_reference_sample(a, b, 0.25)
     vals, rows_used, secs = [], 0, 0.0
     for _ in range(args.steps):
-        v, threads, rows_used, dt = cpu_reference_sample(a, b, 2.0)
+        v, threads, rows_used, dt = cpu_reference_sample(a, b, 4.0)
         vals.append(v)
         secs += dt
     value = statistics.median(vals)
-    sample = f"{rows_used} of {M} rows of A x full B (8192x8192), fp32 einsum, per step"
+    sample = f"{rows_used} rows of A (M={M}) x full B (8192x8192), fp32 einsum, per step"
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
@@ -185,7 +209,7 @@ def run_reference_arm(args):
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--mode", choices=["auto", "1cta", "2cta"], default="2cta")
@@ -239,11 +263,13 @@ def main() -> int:
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    sampler.mark("t_start")
     ev0.record(stream)
     for _ in range(args.steps):
         plan.execute()
     ev1.record(stream)
     torch.cuda.synchronize()
+    sampler.mark("t_end")
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
@@ -293,7 +319,7 @@ def main() -> int:
         if world == 1 and not args.no_cpu_baseline:
             v, threads, rows, dt = cpu_reference_sample(a_cpu, b_cpu, args.cpu_budget_s)
             cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"{rows} of {M} rows of A x full B, fp32 einsum (reference CPU "
+                   "sample": f"{rows} rows of A (M={M}) x full B, fp32 einsum (reference CPU "
                              f"check path), {dt:.1f} s"}
         peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
         traffic = profile_traffic()

@@ -1,0 +1,68 @@
+"""N-sharded GEMM over NCCL on every visible GPU (skipped with fewer than 2).
+
+Each rank runs the B200 kernel on its output columns; the full matrix is
+gathered with one NCCL all-gather and compared with the CPU oracle.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import sys
+    from pathlib import Path
+    repo = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(repo / "gb300-gemm-anatomy_b200"))
+    sys.path.insert(0, str(repo))
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from b200gemm import check, dist as bdist, operands
+        from oracle import oracle
+        m, n, k = 384, 1000, 256
+        a, b = operands.uniform_operands(m, n, k, seed=12)
+        n0, n1 = bdist.shard_bounds(n, world, rank)
+        sg = bdist.ShardedGemm(a.to(dev), b[n0:n1].contiguous().to(dev), n)
+        full = sg.run("full")
+        sg.synchronize()
+        torch.cuda.synchronize()
+        ref = torch.from_numpy(oracle.gemm_tn_f64(a, b))
+        check.bf16_tolerance_check(f"rank {rank}", ref, full.cpu(), k, 1.0, 1.0)
+        sg.destroy()
+        q.put((rank, True, ""))
+    except Exception as exc:
+        q.put((rank, False, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_gemm_nccl_gather():
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in res), res
