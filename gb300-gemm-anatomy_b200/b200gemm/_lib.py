@@ -30,6 +30,7 @@ OUT_F32 = 1
 MODE_AUTO = 0
 MODE_1CTA = 1
 MODE_2CTA = 2
+MODE_2CTA_M512 = 3
 
 STREAM_LDGSTS = 0
 STREAM_TMA = 1

@@ -131,6 +131,31 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
     return ok != 0;
 }
 
+// Same probes with a suspend-time hint: a warp whose phase is not complete is
+// parked by the hardware for up to `hint_ns` (woken early when the phase
+// completes) instead of spinning, which keeps long waits off the issue slots
+// and out of the power budget.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster_hint(uint32_t bar, uint32_t parity,
+                                                           uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
+
 // Bounded phase wait. Returns true when the phase with `parity` completed.
 // Gives up (returns false, records `code` in *status) when `timeout_ns`
 // elapses or when another role of the launch has already failed, so a broken
@@ -138,14 +163,17 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status,
                                           uint64_t timeout_ns, int code) {
+    // Suspend hint: 20 us, far below the timeout, far above one pipeline step.
+    constexpr uint32_t kHintNs = 20000;
     auto probe = [&]() {
-        return kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+        return kClusterScope ? mbar_try_wait_cluster_hint(bar, parity, kHintNs)
+                             : mbar_try_wait_hint(bar, parity, kHintNs);
     };
     if (probe()) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
 #pragma unroll 1
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 4; ++i) {
             if (probe()) return true;
         }
         if (status_failed(status)) return false;

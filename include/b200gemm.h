@@ -57,8 +57,13 @@ enum {
 /* Output element types. */
 enum { B200_OUT_BF16 = 0, B200_OUT_F32 = 1 };
 
-/* GEMM modes. AUTO picks the pair-CTA kernel when it has enough tiles. */
-enum { B200_MODE_AUTO = 0, B200_MODE_1CTA = 1, B200_MODE_2CTA = 2 };
+/* GEMM modes (tile of D per CTA pair or CTA):
+ *   1CTA       128 x 256 per CTA, accumulators double-buffered across tiles
+ *   2CTA       256 x 256 per CTA pair (cta_group::2), double-buffered
+ *   2CTA_M512  512 x 256 per CTA pair: each CTA owns two 128-row accumulators
+ *              that fill TMEM; 25 % fewer L2->SM bytes per FLOP than 2CTA
+ * AUTO picks by shape. */
+enum { B200_MODE_AUTO = 0, B200_MODE_1CTA = 1, B200_MODE_2CTA = 2, B200_MODE_2CTA_M512 = 3 };
 
 /* ------------------------------------------------------------------------ */
 /* Library / device                                                          */
