@@ -212,7 +212,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--mode", choices=["auto", "1cta", "2cta"], default="2cta")
+    ap.add_argument("--mode", choices=["auto", "1cta", "2cta", "2cta_m512"], default="auto")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -44,6 +44,7 @@ constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
 constexpr int kEpiBufBytes = 32 * 128;  // one warp's staging tile: 32 rows x 128 bytes
 constexpr int kTmemCols = 2 * kBN;      // double-buffered accumulator
+constexpr int kQueue = 4;               // tile-id queue slots (producer -> MMA, epilogue, peer)
 
 // kSubM = 128-row accumulators each CTA owns per tile. 1: tile = 128 x 256 per
 // CTA and the two 256-column TMEM slots double-buffer successive tiles.
@@ -64,7 +65,9 @@ struct GemmCfg {
     static constexpr int kEpiOffset = kStages * kStageBytes;
     static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
     static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
-    static constexpr int kBarBytes = (2 * kStages + 4) * 8 + 16;
+    // full[S], empty[S], tfull[2], tempty[2], qfull[Q], qempty[Q], TMEM address, tile-id ring[Q]
+    static constexpr int kBarCount = 2 * kStages + 4 + 2 * kQueue;
+    static constexpr int kBarBytes = kBarCount * 8 + 16 + 4 * kQueue;
     static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
     static_assert(kStageBytes % 1024 == 0, "ring slots must keep 1024-byte alignment");
     static_assert(kSmemBytes <= 232448, "exceeds the 227 KB opt-in shared memory");
@@ -77,6 +80,9 @@ struct GemmParams {
     int group_m;     // blocks per raster group along the grouped dimension
     int raster_n;    // 0: groups of m-blocks walk all n-blocks; 1: groups of n-blocks walk all m-blocks
     int* status;
+    // Dynamic tile scheduler: [0] next tile id, [1] fetchers that found the end.
+    // Zero before a launch; the last fetcher of every launch zeroes it again.
+    int* tile_counter;
     unsigned long long timeout_ns;
     // Optional timeline (nullptr = off): per CTA kTraceSlots %globaltimer stamps.
     unsigned long long* trace;
@@ -134,12 +140,15 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
     const uint32_t empty0 = full0 + 8 * kStages;
     const uint32_t tfull0 = empty0 + 8 * kStages;
     const uint32_t tempty0 = tfull0 + 16;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + (2 * kStages + 4) * 8);
+    const uint32_t qfull0 = tempty0 + 16;
+    const uint32_t qempty0 = qfull0 + 8 * kQueue;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + C::kBarCount * 8);
+    volatile int* ring = reinterpret_cast<volatile int*>(smem + C::kBarOffset + C::kBarCount * 8 + 16);
+    const uint32_t ring_addr = smem_u32(const_cast<int*>(ring));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t rank = kPair ? cluster_ctarank() : 0;
-    const int cluster_id = blockIdx.x / kCtaGroup;
     const int num_clusters = gridDim.x / kCtaGroup;
 
     if (threadIdx.x == 0) {
@@ -150,6 +159,12 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull0 + 8 * a, 1);
             mbar_init(tempty0 + 8 * a, kEpiWarps * kCtaGroup);
+        }
+        // A queued tile id is read by the MMA issuer and 4 epilogue warps of the
+        // leader, and in pair mode also by the peer's producer and 4 epilogue warps.
+        for (int q = 0; q < kQueue; ++q) {
+            mbar_init(qfull0 + 8 * q, 1);
+            mbar_init(qempty0 + 8 * q, kPair ? 10 : 5);
         }
         fence_barrier_init();
     }
@@ -168,12 +183,54 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
     if (threadIdx.x == 0) trace_stamp(p, 1);
 
+    // Tile-id queue. The leader's producer fetches ids from the global counter
+    // in launch-wide order (so tiles sharing A/B panels run at the same time
+    // whatever the drift between pairs) and publishes them to every consumer;
+    // -1 ends the walk. Consumers read a slot and release it at once.
+    auto queue_wait = [&](uint32_t qs, uint32_t qph, int code) -> bool {
+        return mbar_wait<kPair>(qfull0 + 8 * qs, qph, p.status, p.timeout_ns, code);
+    };
+    auto queue_release = [&](uint32_t qs) {
+        if constexpr (kPair) mbar_arrive_cluster(mapa_shared(qempty0 + 8 * qs, 0));
+        else mbar_arrive(qempty0 + 8 * qs);
+    };
+
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (elect_one()) {
-            uint32_t stage = 0, phase = 0;
+            uint32_t stage = 0, phase = 0, qs = 0, qph = 0;
             bool ok = true;
-            for (int t = cluster_id; ok && t < p.num_tiles; t += num_clusters) {
+            while (ok) {
+                int t;
+                if (rank == 0) {
+                    // Fetch the next tile id and publish it.
+                    if (!mbar_wait(qempty0 + 8 * qs, qph ^ 1, p.status, p.timeout_ns,
+                                   B200_DEV_TIMEOUT_PRODUCER)) {
+                        break;
+                    }
+                    t = atomicAdd(&p.tile_counter[0], 1);
+                    if (t >= p.num_tiles) {
+                        t = -1;
+                        __threadfence();
+                        if (atomicAdd(&p.tile_counter[1], 1) == num_clusters - 1) {
+                            // Every fetcher has made its last increment: re-arm the counter.
+                            atomicExch(&p.tile_counter[0], 0);
+                            atomicExch(&p.tile_counter[1], 0);
+                        }
+                    }
+                    ring[qs] = t;
+                    if constexpr (kPair) {
+                        st_shared_cluster_u32(mapa_shared(ring_addr + 4 * qs, 1), static_cast<uint32_t>(t));
+                        mbar_arrive_cluster(mapa_shared(qfull0 + 8 * qs, 1));
+                    }
+                    mbar_arrive(qfull0 + 8 * qs);
+                } else {
+                    if (!queue_wait(qs, qph, B200_DEV_TIMEOUT_PRODUCER)) break;
+                    t = ring[qs];
+                    queue_release(qs);
+                }
+                if (++qs == kQueue) { qs = 0; qph ^= 1; }
+                if (t < 0) break;
                 int mb, nb;
                 tile_coords(t, p, mb, nb);
                 const int a_row = mb * C::kTileM + static_cast<int>(rank) * C::kARows;
@@ -209,9 +266,14 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
             constexpr uint32_t idesc = idesc_bf16_f32(kRowsPerCta * kCtaGroup, kBN);
             // Accumulator unit u (kSubM per tile) lives in TMEM slot u & 1; its
             // barriers' phase flips every second unit.
-            uint32_t stage = 0, phase = 0, unit = 0;
+            uint32_t stage = 0, phase = 0, unit = 0, qs = 0, qph = 0;
             bool ok = true;
-            for (int t = cluster_id; ok && t < p.num_tiles; t += num_clusters) {
+            while (ok) {
+                if (!queue_wait(qs, qph, B200_DEV_TIMEOUT_MMA_FULL)) break;
+                const int t = ring[qs];
+                queue_release(qs);
+                if (++qs == kQueue) { qs = 0; qph ^= 1; }
+                if (t < 0) break;
                 for (int kb = 0; ok && kb < p.num_k_blocks; ++kb) {
                     if (!mbar_wait(full0 + 8 * stage, phase, p.status, p.timeout_ns,
                                    B200_DEV_TIMEOUT_MMA_FULL)) {
@@ -270,10 +332,16 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         // ----------------------------------------------------------- epilogue
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const uint32_t stage_buf0 = sbase + C::kEpiOffset + q * 2 * kEpiBufBytes;
-        uint32_t unit = 0, buf = 0;
+        uint32_t unit = 0, buf = 0, qs = 0, qph = 0;
         int local_tile = 0;
         bool ok = true;
-        for (int t = cluster_id; ok && t < p.num_tiles; t += num_clusters, ++local_tile) {
+        for (; ok; ++local_tile) {
+            if (!queue_wait(qs, qph, B200_DEV_TIMEOUT_EPILOGUE)) break;
+            const int t = ring[qs];
+            __syncwarp();
+            if (lane == 0) queue_release(qs);
+            if (++qs == kQueue) { qs = 0; qph ^= 1; }
+            if (t < 0) break;
             int mb, nb;
             tile_coords(t, p, mb, nb);
             const int col0 = nb * kBN;
@@ -396,6 +464,8 @@ struct B200Plan {
 
 namespace b200 {
 
+constexpr size_t kPlanWordsBytes = 16;  // status word, pad, 2-int tile counter
+
 static int check_shape(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dtype, int mode) {
     if (out_dtype != B200_OUT_BF16 && out_dtype != B200_OUT_F32) {
         set_error("out_dtype=%d is neither B200_OUT_BF16 nor B200_OUT_F32", out_dtype);
@@ -435,24 +505,40 @@ static int check_shape(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dty
     return B200_OK;
 }
 
-// Raster of the persistent tile walk. Overridable for tuning with
+// Raster of the tile walk: tile ids are handed out in launch-wide order, in
+// groups of `group` m-blocks that each walk every n-block. The group is sized
+// so that its A panel (group x tile_m x K bf16) stays near a fixed L2 budget:
+// measured at 8192^3 and 16384^3 (512 x 256 tiles) the least DRAM traffic came
+// with 8 and 4 m-blocks, i.e. a 64 MiB panel (0.82 GB and 7.7 GB read); 256 x
+// 256 and 128 x 256 tiles prefer half of that. Overridable for tuning with
 // B200_GEMM_GROUP (blocks per group, >= 1) and B200_GEMM_RASTER ("m" or "n").
-static void raster_for(const GemmParams& p, int* group, int* raster_n) {
-    // 8 m-blocks per group: the 74-148 tiles in flight then span ~8 x 9 blocks,
-    // which measured the least DRAM traffic at 8192^3 (1.11 GB vs 1.26 GB at 16).
-    *group = 8;
+static void raster_for(const GemmParams& p, int tile_m, int sub_m, int* group, int* raster_n) {
+    const double budget = (sub_m == 2 ? 64.0 : 32.0) * 1024 * 1024;
+    const double panel = static_cast<double>(tile_m) * std::max(p.k, 64) * 2.0;
+    int g = static_cast<int>(budget / panel + 0.5);
+    g = std::max(2, std::min(16, g));
+    *group = std::min(g, std::max(p.num_m_blocks, 1));
     *raster_n = 0;
-    if (const char* g = std::getenv("B200_GEMM_GROUP")) {
-        const int v = std::atoi(g);
+    if (const char* e = std::getenv("B200_GEMM_GROUP")) {
+        const int v = std::atoi(e);
         if (v >= 1 && v <= 4096) *group = v;
     }
     if (const char* r = std::getenv("B200_GEMM_RASTER")) *raster_n = (r[0] == 'n' || r[0] == 'N');
-    (void)p;
 }
 
-static int resolve_mode(int mode, int64_t m) {
+// AUTO: measured on B200 (8192^3 and the LLM projection shapes). Small
+// problems that cannot fill the pairs run 1-CTA tiles; the 512 x 256 pair tile
+// needs at least four waves of tiles to amortise its coarser quantisation,
+// otherwise 256 x 256 pair tiles win.
+static int resolve_mode(int mode, int64_t m, int64_t n, int sm_count) {
     if (mode != B200_MODE_AUTO) return mode;
-    return m >= 256 ? B200_MODE_2CTA : B200_MODE_1CTA;
+    const int64_t pairs = std::max(sm_count / 2, 1);
+    const int64_t nb = (n + kBN - 1) / kBN;
+    const int64_t tiles_2cta = ((m + 255) / 256) * nb;
+    if (m < 256 || tiles_2cta < pairs / 2) return B200_MODE_1CTA;
+    const int64_t tiles_m512 = ((m + 511) / 512) * nb;
+    if (tiles_m512 >= 4 * pairs) return B200_MODE_2CTA_M512;
+    return B200_MODE_2CTA;
 }
 
 static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
@@ -505,7 +591,7 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
     plan->device = device;
     plan->stream = static_cast<cudaStream_t>(stream);
     plan->out_f32 = out_dtype == B200_OUT_F32;
-    const int resolved = resolve_mode(mode, m);
+    const int resolved = resolve_mode(mode, m, n, props.sm_count);
     plan->cta_group = resolved == B200_MODE_1CTA ? 1 : 2;
     plan->sub_m = resolved == B200_MODE_2CTA_M512 ? 2 : 1;
     plan->empty_problem = empty;
@@ -519,21 +605,23 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
     p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
     p.num_k_blocks = static_cast<int>((k + kBK - 1) / kBK);
     p.num_tiles = p.num_m_blocks * p.num_n_blocks;
-    raster_for(p, &p.group_m, &p.raster_n);
+    raster_for(p, tile_m, plan->sub_m, &p.group_m, &p.raster_n);
     p.timeout_ns = wait_timeout_ns();
 
-    cudaError_t err = cudaMalloc(&plan->d_status, sizeof(int));
+    // Device words of the plan: [0] status, [2..3] tile scheduler counter.
+    cudaError_t err = cudaMalloc(&plan->d_status, kPlanWordsBytes);
     if (err != cudaSuccess) {
         delete plan;
         return cuda_fail("cudaMalloc(status word)", err);
     }
-    err = cudaMemset(plan->d_status, 0, sizeof(int));
+    err = cudaMemset(plan->d_status, 0, kPlanWordsBytes);
     if (err != cudaSuccess) {
         cudaFree(plan->d_status);
         delete plan;
         return cuda_fail("cudaMemset(status word)", err);
     }
     p.status = plan->d_status;
+    p.tile_counter = plan->d_status + 2;
 
     int slots = 0;
     if (!empty) {
@@ -715,7 +803,8 @@ int b200_stream_synchronize(B200Plan* plan) {
     int status = 0;
     B200_CUDA_TRY(cudaMemcpy(&status, plan->d_status, sizeof(int), cudaMemcpyDeviceToHost));
     if (status != 0) {
-        B200_CUDA_TRY(cudaMemset(plan->d_status, 0, sizeof(int)));
+        // An aborted launch may leave the tile counter mid-walk: re-arm it too.
+        B200_CUDA_TRY(cudaMemset(plan->d_status, 0, b200::kPlanWordsBytes));
         b200::set_error("GEMM kernel reported device status 0x%x (%s)", status,
                         status == B200_DEV_BAD_LAUNCH ? "launch contract violated"
                                                       : "bounded wait timed out");
@@ -787,10 +876,10 @@ int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, voi
 // ---------------------------------------------------------------------------
 // Allocation-free entry point.
 //
-// b200_gemm_noalloc runs the same kernel as b200_gemm, but the one piece of
-// device scratch the kernel needs -- its status word, where bounded waits
-// record a timeout -- lives in the file-scope array below instead of a
-// cudaMalloc'd buffer. Callers that cannot allocate device memory use it:
+// b200_gemm_noalloc runs the same kernel as b200_gemm, but the device scratch
+// the kernel needs -- its status word, where bounded waits record a timeout,
+// and the tile scheduler's counter -- lives in the file-scope array below
+// instead of a cudaMalloc'd buffer. Callers that cannot allocate device memory use it:
 // applications that hand all device memory to their own pool at start-up and
 // forbid later driver allocations, and latency-critical paths that must not
 // take the implicit device-wide synchronisation cudaMalloc/cudaFree imply.
@@ -833,7 +922,7 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
                            int device, const DeviceProps& props, int* status) {
     plan->device = device;
     plan->out_f32 = out_dtype == B200_OUT_F32;
-    const int resolved = resolve_mode(mode, m);
+    const int resolved = resolve_mode(mode, m, n, props.sm_count);
     plan->cta_group = resolved == B200_MODE_1CTA ? 1 : 2;
     plan->sub_m = resolved == B200_MODE_2CTA_M512 ? 2 : 1;
     plan->empty_problem = (m == 0 || n == 0);
@@ -847,9 +936,10 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
     p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
     p.num_k_blocks = static_cast<int>((k + kBK - 1) / kBK);
     p.num_tiles = p.num_m_blocks * p.num_n_blocks;
-    raster_for(p, &p.group_m, &p.raster_n);
+    raster_for(p, tile_m, plan->sub_m, &p.group_m, &p.raster_n);
     p.timeout_ns = wait_timeout_ns();
     p.status = status;
+    p.tile_counter = status + 2;
     if (plan->empty_problem) return B200_OK;
     int rc = encode_tmap_2d(&plan->tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, m, k, k,
                             kRowsPerCta * plan->sub_m, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -895,9 +985,9 @@ extern "C" int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a,
         b200::set_error("K=0 with a non-empty output is not supported (D would be all zeros)");
         return B200_ERR_UNSUPPORTED;
     }
-    // This launch needs one status word of scratch; refuse anything that would
-    // not fit the static array.
-    constexpr size_t kNeeded = sizeof(int);
+    // This launch needs 16 bytes of scratch (status word and the tile
+    // scheduler's counter); refuse anything that would not fit the static array.
+    constexpr size_t kNeeded = b200::kPlanWordsBytes;
     if (kNeeded > b200::kNoAllocScratchBytes) {
         b200::set_error("b200_gemm_noalloc needs %zu bytes of scratch, the static array holds %zu",
                         kNeeded, b200::kNoAllocScratchBytes);
@@ -924,8 +1014,9 @@ extern "C" int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a,
     if (rc != B200_OK) return rc;
     if (plan.empty_problem) return B200_OK;
 
-    // The array keeps the previous call's contents: the status word must start at zero.
-    B200_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), plan.stream));
+    // The array keeps the previous call's contents: status word and tile
+    // counter must start at zero.
+    B200_CUDA_TRY(cudaMemsetAsync(status, 0, b200::kPlanWordsBytes, plan.stream));
     rc = b200::plan_launch(&plan, plan.stream);
     if (rc != B200_OK) return rc;
     int host_status = 0;

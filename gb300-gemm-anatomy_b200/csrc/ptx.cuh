@@ -110,6 +110,11 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
                  ::"r"(cluster_bar) : "memory");
 }
 
+// 32-bit store into the shared memory of any CTA of the cluster.
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(

@@ -152,7 +152,9 @@ int b200_gemm_plan_create_ex(int64_t m, int64_t n, int64_t k, const void* a, con
  * launch on the plan's stream. */
 int b200_gemm_plan_execute(B200Plan* plan);
 
-/* Same launch on another stream (e.g. inside a CUDA-graph capture). */
+/* Same launch on another stream (e.g. inside a CUDA-graph capture). Launches of
+ * one plan must not overlap on the GPU: they share its status word and tile
+ * counter. */
 int b200_gemm_plan_execute_on(B200Plan* plan, void* stream);
 
 /* Replaces p35_stream_synchronize (cublaslt_bridge_p35.cu:987): waits for the
@@ -174,18 +176,19 @@ int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, voi
 
 /* Allocation-free GEMM. No counterpart in the reference. Same arguments,
  * kernel and synchronous behaviour as b200_gemm, but it calls no cudaMalloc,
- * cudaFree or other allocating routine: the kernel's only scratch (its 4-byte
- * status word for bounded-wait timeouts) lives in a 256-byte static device
+ * cudaFree or other allocating routine: the kernel's only scratch (16 bytes:
+ * the status word for bounded-wait timeouts and the tile scheduler's counter)
+ * lives in a 256-byte static device
  * array of the library, which every GPU that loads the library holds until
  * exit. For callers that cannot allocate device memory -- programs that give
  * all device memory to their own pool up front, or paths that must avoid the
  * device-wide synchronisation cudaMalloc/cudaFree imply.
  * The first call on a device looks up the array's device address (with that
  * device current); make that first call before any stream capture. Calls
- * share the array: each clears the status word before its launch, and calls
+ * share the array: each clears those 16 bytes before its launch, and calls
  * that overlap on the GPU (other streams, other threads) race on it. A launch
  * whose scratch need exceeded the array would be refused with
- * B200_ERR_UNSUPPORTED; this kernel needs 4 bytes whatever M, N and K are. */
+ * B200_ERR_UNSUPPORTED; this kernel needs 16 bytes whatever M, N and K are. */
 int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
                       int64_t ldd, int out_dtype, int mode, void* stream);
 

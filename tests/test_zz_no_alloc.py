@@ -3,7 +3,7 @@
 Some callers cannot allocate device memory (they give all of it to their own
 pool up front, or must not take the device-wide synchronisation that
 cudaMalloc/cudaFree imply). b200_gemm_noalloc serves them: it keeps the
-kernel's only scratch -- its status word -- in a static device array of the
+kernel's only scratch -- its status word and tile counter -- in a static device array of the
 library. This test calls it through the C ABI twice in a row, on different
 operands, and checks each result against the existing entry point b200_gemm
 (bit-identical: same kernel) and against the CPU oracle with the bf16
