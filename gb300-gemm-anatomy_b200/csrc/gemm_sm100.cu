@@ -27,6 +27,7 @@
 // and signals the leader's full barrier; the leader's commits are sent to each
 // CTA's barrier separately (two unicast commits, no multicast anywhere).
 #include <algorithm>
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -506,16 +507,15 @@ static int check_shape(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dty
 }
 
 // Raster of the tile walk: tile ids are handed out in launch-wide order, in
-// groups of `group` m-blocks that each walk every n-block. The group is sized
-// so that its A panel (group x tile_m x K bf16) stays near a fixed L2 budget:
-// measured at 8192^3 and 16384^3 (512 x 256 tiles) the least DRAM traffic came
-// with 8 and 4 m-blocks, i.e. a 64 MiB panel (0.82 GB and 7.7 GB read); 256 x
-// 256 and 128 x 256 tiles prefer half of that. Overridable for tuning with
-// B200_GEMM_GROUP (blocks per group, >= 1) and B200_GEMM_RASTER ("m" or "n").
+// groups of `group` m-blocks that each walk every n-block. Measured on B200
+// with ncu DRAM counters (8192^3, 16384^3, 8192 x {14336, 128256} x 4096):
+// the least traffic came when a group spans ~4096 rows of A, capped so the
+// group's A panel stays within 64 MiB (2048 rows at K = 16384). Overridable
+// for tuning with B200_GEMM_GROUP (>= 1) and B200_GEMM_RASTER ("m" or "n").
 static void raster_for(const GemmParams& p, int tile_m, int sub_m, int* group, int* raster_n) {
-    const double budget = (sub_m == 2 ? 64.0 : 32.0) * 1024 * 1024;
-    const double panel = static_cast<double>(tile_m) * std::max(p.k, 64) * 2.0;
-    int g = static_cast<int>(budget / panel + 0.5);
+    (void)sub_m;
+    const double rows = std::min(4096.0, 64.0 * 1024 * 1024 / (2.0 * std::max(p.k, 64)));
+    int g = static_cast<int>(rows / tile_m + 0.5);
     g = std::max(2, std::min(16, g));
     *group = std::min(g, std::max(p.num_m_blocks, 1));
     *raster_n = 0;
@@ -526,18 +526,26 @@ static void raster_for(const GemmParams& p, int tile_m, int sub_m, int* group, i
     if (const char* r = std::getenv("B200_GEMM_RASTER")) *raster_n = (r[0] == 'n' || r[0] == 'N');
 }
 
-// AUTO: measured on B200 (8192^3 and the LLM projection shapes). Small
-// problems that cannot fill the pairs run 1-CTA tiles; the 512 x 256 pair tile
-// needs at least four waves of tiles to amortise its coarser quantisation,
-// otherwise 256 x 256 pair tiles win.
+// AUTO: small problems that cannot fill the pairs run 1-CTA tiles. Otherwise
+// the pair-tile shape with the better score wins, score = waves / ceil(waves)
+// (the fraction of the last wave that is busy) x 1.03 for 512 x 256 tiles,
+// whose smaller L2->SM traffic measured ~3 % more work per joule; 512 x 256
+// needs at least four waves. Measured on B200: 8192^3, 16384^3 and
+// 8192 x 128256 x 4096 pick 512 x 256; 4096^3 and 8192 x {4096, 14336} x 4096
+// pick 256 x 256.
 static int resolve_mode(int mode, int64_t m, int64_t n, int sm_count) {
     if (mode != B200_MODE_AUTO) return mode;
-    const int64_t pairs = std::max(sm_count / 2, 1);
+    const double pairs = std::max(sm_count / 2, 1);
     const int64_t nb = (n + kBN - 1) / kBN;
     const int64_t tiles_2cta = ((m + 255) / 256) * nb;
     if (m < 256 || tiles_2cta < pairs / 2) return B200_MODE_1CTA;
     const int64_t tiles_m512 = ((m + 511) / 512) * nb;
-    if (tiles_m512 >= 4 * pairs) return B200_MODE_2CTA_M512;
+    auto busy = [&](int64_t tiles) {
+        const double w = static_cast<double>(tiles) / pairs;
+        return w / std::ceil(w);
+    };
+    if (tiles_m512 >= 4 * pairs && 1.03 * busy(tiles_m512) > busy(tiles_2cta))
+        return B200_MODE_2CTA_M512;
     return B200_MODE_2CTA;
 }
 
