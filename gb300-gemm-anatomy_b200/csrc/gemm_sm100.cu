@@ -201,15 +201,18 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         if (elect_one()) {
             uint32_t stage = 0, phase = 0, qs = 0, qph = 0;
             bool ok = true;
+            // The leader fetches tile ids one tile ahead so the atomic's round
+            // trip overlaps the current tile's loads instead of delaying the next.
+            int next = (rank == 0) ? atomicAdd(&p.tile_counter[0], 1) : -1;
             while (ok) {
                 int t;
                 if (rank == 0) {
-                    // Fetch the next tile id and publish it.
+                    // Publish the prefetched tile id.
                     if (!mbar_wait(qempty0 + 8 * qs, qph ^ 1, p.status, p.timeout_ns,
                                    B200_DEV_TIMEOUT_PRODUCER)) {
                         break;
                     }
-                    t = atomicAdd(&p.tile_counter[0], 1);
+                    t = next;
                     if (t >= p.num_tiles) {
                         t = -1;
                         __threadfence();
@@ -218,6 +221,8 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                             atomicExch(&p.tile_counter[0], 0);
                             atomicExch(&p.tile_counter[1], 0);
                         }
+                    } else {
+                        next = atomicAdd(&p.tile_counter[0], 1);
                     }
                     ring[qs] = t;
                     if constexpr (kPair) {
@@ -275,53 +280,81 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 queue_release(qs);
                 if (++qs == kQueue) { qs = 0; qph ^= 1; }
                 if (t < 0) break;
-                for (int kb = 0; ok && kb < p.num_k_blocks; ++kb) {
-                    if (!mbar_wait(full0 + 8 * stage, phase, p.status, p.timeout_ns,
+                // MMAs of row half `sm` for k-slice `kb` held in ring slot `st`; the
+                // first k-slice of a half waits for its TMEM slot, the last one
+                // signals the epilogue.
+                auto issue_sub = [&](int sm, uint32_t st, int kb) -> bool {
+                    const uint32_t u = unit + sm;
+                    const uint32_t slot = u & 1;
+                    if (kb == 0) {
+                        if (!mbar_wait<kPair>(tempty0 + 8 * slot, ((u >> 1) & 1) ^ 1, p.status,
+                                              p.timeout_ns, B200_DEV_TIMEOUT_MMA_TMEM)) {
+                            return false;
+                        }
+                        tc_fence_after();
+                    }
+                    const uint32_t sa = sbase + st * C::kStageBytes;
+                    const uint32_t sb = sa + C::kABytes;
+                    const uint32_t d_tmem = tmem_base + slot * kBN;
+                    const uint32_t a_sub = sa + sm * (kRowsPerCta * kBK * 2);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k) {
+                        umma_bf16<kCtaGroup>(d_tmem, smem_desc_sw128(a_sub + 32 * k),
+                                             smem_desc_sw128(sb + 32 * k), idesc,
+                                             (kb | k) != 0 ? 1u : 0u);
+                    }
+                    if (kb == p.num_k_blocks - 1) {
+                        const uint32_t tb = tfull0 + 8 * slot;
+                        if constexpr (!kPair) {
+                            umma_commit<1>(tb);
+                        } else {
+                            umma_commit<2>(mapa_shared(tb, 0));
+                            umma_commit<2>(mapa_shared(tb, 1));
+                        }
+                    }
+                    return true;
+                };
+                auto wait_full = [&](uint32_t st, uint32_t ph) -> bool {
+                    if (!mbar_wait(full0 + 8 * st, ph, p.status, p.timeout_ns,
                                    B200_DEV_TIMEOUT_MMA_FULL)) {
-                        ok = false;
-                        break;
+                        return false;
                     }
                     tc_fence_after();
-                    const uint32_t sa = sbase + stage * C::kStageBytes;
-                    const uint32_t sb = sa + C::kABytes;
-#pragma unroll
-                    for (int sm = 0; sm < kSubM; ++sm) {
-                        const uint32_t u = unit + sm;
-                        const uint32_t slot = u & 1;
-                        if (kb == 0) {
-                            if (!mbar_wait<kPair>(tempty0 + 8 * slot, ((u >> 1) & 1) ^ 1, p.status,
-                                                  p.timeout_ns, B200_DEV_TIMEOUT_MMA_TMEM)) {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                        }
-                        const uint32_t d_tmem = tmem_base + slot * kBN;
-                        const uint32_t a_sub = sa + sm * (kRowsPerCta * kBK * 2);
-#pragma unroll
-                        for (int k = 0; k < kBK / 16; ++k) {
-                            umma_bf16<kCtaGroup>(d_tmem, smem_desc_sw128(a_sub + 32 * k),
-                                                 smem_desc_sw128(sb + 32 * k), idesc,
-                                                 (kb | k) != 0 ? 1u : 0u);
-                        }
-                        if (kb == p.num_k_blocks - 1) {
-                            const uint32_t tb = tfull0 + 8 * slot;
-                            if constexpr (!kPair) {
-                                umma_commit<1>(tb);
-                            } else {
-                                umma_commit<2>(mapa_shared(tb, 0));
-                                umma_commit<2>(mapa_shared(tb, 1));
-                            }
-                        }
-                    }
-                    if (!ok) break;
-                    const uint32_t eb = empty0 + 8 * stage;
+                    return true;
+                };
+                auto release_stage = [&](uint32_t st) {
+                    const uint32_t eb = empty0 + 8 * st;
                     if constexpr (!kPair) {
                         umma_commit<1>(eb);
                     } else {
                         umma_commit<2>(mapa_shared(eb, 0));
                         umma_commit<2>(mapa_shared(eb, 1));
                     }
+                };
+                // Head start (two row halves): the first half runs over the first
+                // `head` k-slices while the epilogue is still draining the second
+                // half's slot; those ring slots are held until the second half has
+                // used them too.
+                const int head = kSubM == 2 ? min(kStages, p.num_k_blocks) : 0;
+                if (head > 0) {
+                    uint32_t st = stage, ph = phase;
+                    for (int kb = 0; ok && kb < head; ++kb) {
+                        ok = wait_full(st, ph) && issue_sub(0, st, kb);
+                        if (++st == kStages) { st = 0; ph ^= 1; }
+                    }
+                    for (int kb = 0; ok && kb < head; ++kb) {
+                        ok = issue_sub(1, stage, kb);
+                        if (!ok) break;
+                        release_stage(stage);
+                        if (++stage == kStages) { stage = 0; phase ^= 1; }
+                    }
+                }
+                for (int kb = head; ok && kb < p.num_k_blocks; ++kb) {
+                    ok = wait_full(stage, phase);
+#pragma unroll
+                    for (int sm = 0; ok && sm < kSubM; ++sm) ok = issue_sub(sm, stage, kb);
+                    if (!ok) break;
+                    release_stage(stage);
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
                 }
                 unit += kSubM;
@@ -348,8 +381,8 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
             const int col0 = nb * kBN;
             for (int sm = 0; sm < kSubM; ++sm, ++unit) {
                 const uint32_t slot = unit & 1;
-                if (!mbar_wait<kPair>(tfull0 + 8 * slot, (unit >> 1) & 1, p.status, p.timeout_ns,
-                                      B200_DEV_TIMEOUT_EPILOGUE)) {
+                if (!mbar_wait<kPair, true>(tfull0 + 8 * slot, (unit >> 1) & 1, p.status,
+                                            p.timeout_ns, B200_DEV_TIMEOUT_EPILOGUE)) {
                     ok = false;
                     break;
                 }
@@ -358,32 +391,8 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 const int row0 = mb * C::kTileM + static_cast<int>(rank) * C::kARows +
                                  sm * kRowsPerCta + q * 32;
                 const uint32_t t_row = tmem_base + slot * kBN + (static_cast<uint32_t>(q * 32) << 16);
-#pragma unroll 1
-                for (int c = 0; c < kChunks; ++c) {
-                    uint32_t packed[32];
-                    if constexpr (kOutF32) {
-                        tmem_ld_32x32b_x32(t_row + c * 32, packed);
-                        tmem_ld_wait();
-                    } else {
-                        uint32_t r0[32], r1[32];
-                        tmem_ld_32x32b_x32(t_row + c * 64, r0);
-                        tmem_ld_32x32b_x32(t_row + c * 64 + 32, r1);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            packed[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
-                            packed[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
-                        }
-                    }
-                    if (c == kChunks - 1) {
-                        // Accumulator fully read: hand it back before the last stores.
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) {
-                            if constexpr (!kPair) mbar_arrive(tempty0 + 8 * slot);
-                            else mbar_arrive_cluster(mapa_shared(tempty0 + 8 * slot, 0));
-                        }
-                    }
+                // Stage one 32-row x 128-byte chunk of this warp's rows and TMA-store it.
+                auto store_chunk = [&](int c, const uint32_t* packed) {
                     const uint32_t sbuf = stage_buf0 + buf * kEpiBufBytes;
                     if (lane == 0) bulk_wait_group_read<1>();
                     __syncwarp();
@@ -401,6 +410,45 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         bulk_commit_group();
                     }
                     buf ^= 1;
+                };
+                auto release_tmem = [&]() {
+                    // Accumulator fully read: hand it back to the MMA issuer.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if constexpr (!kPair) mbar_arrive(tempty0 + 8 * slot);
+                        else mbar_arrive_cluster(mapa_shared(tempty0 + 8 * slot, 0));
+                    }
+                };
+                if constexpr (kOutF32) {
+#pragma unroll 1
+                    for (int c = 0; c < kChunks; ++c) {
+                        uint32_t packed[32];
+                        tmem_ld_32x32b_x32(t_row + c * 32, packed);
+                        tmem_ld_wait();
+                        if (c == kChunks - 1) release_tmem();
+                        store_chunk(c, packed);
+                    }
+                } else {
+                    // bf16: the whole 256-column row fits in 128 registers once
+                    // packed, so drain TMEM completely first and release it before
+                    // any store; the next tile's MMAs into this slot start sooner.
+                    uint32_t packed[kChunks][32];
+#pragma unroll
+                    for (int c = 0; c < kChunks; ++c) {
+                        uint32_t r0[32], r1[32];
+                        tmem_ld_32x32b_x32(t_row + c * 64, r0);
+                        tmem_ld_32x32b_x32(t_row + c * 64 + 32, r1);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            packed[c][i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+                            packed[c][16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+                        }
+                    }
+                    release_tmem();
+#pragma unroll
+                    for (int c = 0; c < kChunks; ++c) store_chunk(c, packed[c]);
                 }
             }
         }

@@ -165,20 +165,27 @@ __device__ __forceinline__ bool mbar_try_wait_cluster_hint(uint32_t bar, uint32_
 // Gives up (returns false, records `code` in *status) when `timeout_ns`
 // elapses or when another role of the launch has already failed, so a broken
 // pipeline ends the kernel with a readable status instead of a hung GPU.
-template <bool kClusterScope = false>
+// kSleep selects the suspend-time hint: only for waits that are long by design
+// (the epilogue waiting a whole tile for its accumulator). Latency-critical
+// waits (producer, MMA issuer) spin with plain try_wait so they resume the
+// moment the phase completes.
+template <bool kClusterScope = false, bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status,
                                           uint64_t timeout_ns, int code) {
-    // Suspend hint: 20 us, far below the timeout, far above one pipeline step.
     constexpr uint32_t kHintNs = 20000;
     auto probe = [&]() {
-        return kClusterScope ? mbar_try_wait_cluster_hint(bar, parity, kHintNs)
-                             : mbar_try_wait_hint(bar, parity, kHintNs);
+        if constexpr (kSleep) {
+            return kClusterScope ? mbar_try_wait_cluster_hint(bar, parity, kHintNs)
+                                 : mbar_try_wait_hint(bar, parity, kHintNs);
+        } else {
+            return kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+        }
     };
     if (probe()) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
 #pragma unroll 1
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 32; ++i) {
             if (probe()) return true;
         }
         if (status_failed(status)) return false;
