@@ -3,7 +3,7 @@
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 One step = one launch of the persistent tcgen05 GEMM over the whole problem
-(2-CTA mode, bf16 in, fp32 accumulate, bf16 out). N=1 runs the 8192^3 square
+(AUTO mode = 512x256 CTA-pair tiles here; bf16 in, fp32 accumulate, bf16 out). N=1 runs the 8192^3 square
 GEMM of the square-sweep config (inputs N(0,1)*0.1 from seed 1). N>1 is
 N-sharded weak scaling: every rank owns an 8192-column shard of an
 M=8192, N=8192*world, K=8192 GEMM (A replicated, B rows = its output columns,
@@ -52,7 +52,7 @@ def load_peaks():
 
 def profile_traffic():
     """DRAM bytes per launch of the GEMM kernel from the committed ncu summary, if any."""
-    p = REPO / "profiles" / "gemm_tn_sm100_8192_2cta.md"
+    p = REPO / "profiles" / "gemm_tn_sm100_8192_m512.md"
     if not p.is_file():
         return None
     for line in p.read_text().splitlines():
