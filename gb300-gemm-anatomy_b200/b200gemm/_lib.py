@@ -125,6 +125,12 @@ SIGNATURES = {
     "b200_gemm": (_INT, [_I64, _I64, _I64, _P, _P, _P, _I64, _INT, _INT, _P]),
     "b200_gemm_plan_launches": (_I64, [_P]),
     "b200_gemm_plan_set_trace": (_INT, [_P, _P, _I64]),
+    "b200_gemm_plan_set_peers": (_INT, [_P, _INT, ctypes.POINTER(_P)]),
+    "b200_ipc_handle_size": (ctypes.c_size_t, []),
+    "b200_peer_buffer_alloc": (_INT, [_I64, ctypes.POINTER(_P), _P]),
+    "b200_peer_buffer_free": (_INT, [_P]),
+    "b200_peer_open": (_INT, [_P, ctypes.POINTER(_P)]),
+    "b200_peer_close": (_INT, [_P]),
     "b200_gemm_noalloc": (_INT, [_I64, _I64, _I64, _P, _P, _P, _I64, _INT, _INT, _P]),
     "b200_fill_pattern": (_INT, [_P, _I64, _P]),
     "b200_stream_plan_create": (_INT, [ctypes.POINTER(StreamConfig), _P, _I64, _INT,

@@ -4,22 +4,29 @@ The reference has no multi-GPU path (its AGENTS.md rules out multi-GPU); this
 layer is new. Each rank owns the output columns [n0, n1) given by
 `b200_shard_range` (ceil(N/world) rounded up to 16 columns, the last shard
 takes the remainder), holds A (M x K, replicated) and its B rows B[n0:n1], and
-runs the single-GPU persistent kernel on them. No collective runs unless the
-caller asks for the full matrix:
+runs the single-GPU persistent kernel on them. The full matrix is produced
+only when the caller asks for it:
 
   gather="none"    D shard M x (n1-n0) on this rank (weak-scaling path)
   gather="blocks"  NCCL all-gather of the padded shards into [world, M, W]
-                   (W = shard width), one collective, no re-layout
   gather="full"    the same, then one re-layout to row-major M x N
+  p2p=True         fused gather: the GEMM's epilogue writes every output chunk
+                   into every rank's row-major M x N buffer over NVLink (plain
+                   16-byte stores through CUDA IPC mappings), so the exchange
+                   overlaps the math tile by tile and needs no re-layout; one
+                   NCCL all-reduce of a scalar then orders the ranks.
 
 One process per GPU; the process group is torch.distributed over NCCL (or
 gloo for CPU tests of the host logic, with `local_gemm` injected).
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from ._lib import shard_range
 
 SHARD_GRANULE = 16
@@ -34,11 +41,56 @@ def shard_width(n: int, world: int, granule: int = SHARD_GRANULE) -> int:
     return e - b
 
 
+class _DeviceArray:
+    """__cuda_array_interface__ view of a raw device allocation (int16 elements)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<i2",
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+class PeerBuffer:
+    """This rank's full-matrix output, mapped into every other rank (CUDA IPC)."""
+
+    def __init__(self, m: int, n: int, group=None):
+        self._lib = _lib.load()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        nbytes = m * n * 2
+        hsize = int(self._lib.b200_ipc_handle_size())
+        handle = ctypes.create_string_buffer(hsize)
+        ptr = ctypes.c_void_p()
+        _lib.check(self._lib.b200_peer_buffer_alloc(nbytes, ctypes.byref(ptr), handle),
+                   "b200_peer_buffer_alloc", self._lib)
+        self.ptr = int(ptr.value)
+        self.tensor = torch.as_tensor(_DeviceArray(self.ptr, (m, n)),
+                                      device=torch.device("cuda", torch.cuda.current_device())
+                                      ).view(torch.bfloat16)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle.raw), group=group)
+        self.peers = {}
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                continue
+            q = ctypes.c_void_p()
+            _lib.check(self._lib.b200_peer_open(ctypes.create_string_buffer(h, hsize), ctypes.byref(q)),
+                       "b200_peer_open", self._lib)
+            self.peers[r] = int(q.value)
+
+    def close(self):
+        for q in self.peers.values():
+            self._lib.b200_peer_close(ctypes.c_void_p(q))
+        self.peers = {}
+        if self.ptr:
+            self._lib.b200_peer_buffer_free(ctypes.c_void_p(self.ptr))
+            self.ptr = 0
+
+
 class ShardedGemm:
     """D = A @ B^T with B (and D) split by output columns across the group."""
 
     def __init__(self, a: torch.Tensor, b_shard: torch.Tensor, n_total: int, *, group=None,
-                 out_dtype=torch.bfloat16, mode: str = "auto", local_gemm=None):
+                 out_dtype=torch.bfloat16, mode: str = "auto", local_gemm=None, p2p: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -49,18 +101,34 @@ class ShardedGemm:
                              f"{b_shard.shape[0]} rows")
         self.m = a.shape[0]
         self.width = shard_width(self.n_total, self.world)
-        # Padded to the common shard width so the gather is one equal-size collective.
-        self.block = torch.zeros((self.m, self.width), dtype=out_dtype, device=a.device)
-        self.out = self.block[:, : self.n1 - self.n0]
         self.a, self.b = a, b_shard
         self._plan = None
+        self.p2p = p2p
+        self.peer_buffer = None
+        if p2p:
+            if local_gemm is not None or out_dtype != torch.bfloat16:
+                raise ValueError("the fused gather runs the B200 kernel with bf16 output")
+            if self.n_total % 8 != 0:
+                raise ValueError("the fused gather needs N % 8 == 0 (16-byte rows)")
+            self.peer_buffer = PeerBuffer(self.m, self.n_total, group)
+            self.full = self.peer_buffer.tensor
+            self.out = self.full[:, self.n0:self.n1]
+        else:
+            # Padded to the common shard width so the gather is one equal-size collective.
+            self.block = torch.zeros((self.m, self.width), dtype=out_dtype, device=a.device)
+            self.out = self.block[:, : self.n1 - self.n0]
         if local_gemm is None:
             from .gemm import GemmPlan
             if self.n1 > self.n0 and self.m > 0:
                 self._plan = GemmPlan(a, b_shard, self.out, mode=mode)
+                if p2p:
+                    pitch_off = self.n0 * 2
+                    self._plan.set_peers([self.peer_buffer.peers[r] + pitch_off
+                                          for r in sorted(self.peer_buffer.peers)])
             self._local = self._plan.execute if self._plan is not None else (lambda: None)
         else:
             self._local = lambda: local_gemm(a, b_shard, self.out)
+        self._flag = None
 
     @property
     def launches_per_step(self) -> int:
@@ -68,6 +136,14 @@ class ShardedGemm:
 
     def run(self, gather: str = "none"):
         self._local()
+        if self.p2p:
+            # Order the ranks: after this all-reduce every rank's kernel (and its
+            # peer writes, fenced system-wide before exit) has completed.
+            if self._flag is None:
+                self._flag = torch.zeros(1, dtype=torch.float32, device=self.a.device)
+            if self.world > 1:
+                dist.all_reduce(self._flag, group=self.group)
+            return self.full if gather != "none" else self.out
         if gather == "none":
             return self.out
         if gather not in ("blocks", "full"):
@@ -92,3 +168,10 @@ class ShardedGemm:
         if self._plan is not None:
             self._plan.destroy()
             self._plan = None
+        if self.peer_buffer is not None:
+            # No rank may still be writing into a buffer that is about to go.
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self.peer_buffer.close()
+            self.peer_buffer = None

@@ -81,6 +81,12 @@ class GemmPlan:
     def launches_per_execute(self) -> int:
         return int(self._lib.b200_gemm_plan_launches(self._plan))
 
+    def set_peers(self, peer_ptrs) -> None:
+        """Fused gather: also write every output chunk into these peer buffers."""
+        arr = (ctypes.c_void_p * max(len(peer_ptrs), 1))(*[ctypes.c_void_p(int(q)) for q in peer_ptrs])
+        _lib.check(self._lib.b200_gemm_plan_set_peers(self._plan, len(peer_ptrs), arr),
+                   "b200_gemm_plan_set_peers", self._lib)
+
     TRACE_SLOTS = 64
 
     def enable_trace(self) -> torch.Tensor:

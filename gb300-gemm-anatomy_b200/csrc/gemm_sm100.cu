@@ -45,7 +45,8 @@ constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
 constexpr int kEpiBufBytes = 32 * 128;  // one warp's staging tile: 32 rows x 128 bytes
 constexpr int kTmemCols = 2 * kBN;      // double-buffered accumulator
-constexpr int kQueue = 4;               // tile-id queue slots (producer -> MMA, epilogue, peer)
+constexpr int kQueue = 4;
+constexpr int kMaxPeers = 7;            // fused gather: up to 8 GPUs               // tile-id queue slots (producer -> MMA, epilogue, peer)
 
 // kSubM = 128-row accumulators each CTA owns per tile. 1: tile = 128 x 256 per
 // CTA and the two 256-column TMEM slots double-buffer successive tiles.
@@ -87,6 +88,13 @@ struct GemmParams {
     unsigned long long timeout_ns;
     // Optional timeline (nullptr = off): per CTA kTraceSlots %globaltimer stamps.
     unsigned long long* trace;
+    // Fused gather (N-sharded multi-GPU): every staged output chunk is also
+    // written with 16-byte stores into each peer GPU's copy of the full D, at
+    // the same row/column (peer_d already points at this shard's columns;
+    // the same row pitch as the local D). npeers = 0: off.
+    int npeers;
+    long long ldd;
+    void* peer_d[kMaxPeers];
 };
 
 // Trace slots per CTA: 0 entry, 1 setup done, 2 producer done, 3 MMA done,
@@ -409,6 +417,22 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         tma_store_2d(&tmD, sbuf, col, row0);
                         bulk_commit_group();
                     }
+                    if (p.npeers > 0 && row0 < p.m && col < p.n) {
+                        // Fused gather: 8 lanes cover one 128-byte staged row, so each
+                        // warp store writes four contiguous 128-byte row segments.
+                        constexpr int kElem = 128 / kColsPerChunk;
+                        const int piece = lane & 7;
+                        const int pcol = col + piece * (16 / kElem);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int r = (lane >> 3) + 4 * i;
+                            if (row0 + r >= p.m || pcol >= p.n) continue;
+                            const uint4 v = ld_shared_v4(sbuf + r * 128 + ((piece ^ (r & 7)) << 4));
+                            const long long off = (static_cast<long long>(row0 + r) * p.ldd + pcol) * kElem;
+                            for (int g = 0; g < p.npeers; ++g)
+                                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_d[g]) + off) = v;
+                        }
+                    }
                     buf ^= 1;
                 };
                 auto release_tmem = [&]() {
@@ -453,6 +477,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
             }
         }
         if (lane == 0) bulk_wait_group<0>();
+        if (p.npeers > 0) __threadfence_system();  // peer writes visible before exit
         __syncwarp();
         if (warp == 2 && lane == 0) trace_stamp(p, 4);
     }
@@ -880,6 +905,24 @@ int b200_gemm_plan_destroy(B200Plan* plan) {
     if (err != cudaSuccess) return b200::cuda_fail("cudaFree(status word)", err);
     return B200_OK;
     B200_ABI_GUARD_END
+}
+
+int b200_gemm_plan_set_peers(B200Plan* plan, int npeers, void* const* peer_d) {
+    b200::clear_error();
+    if (plan == nullptr || npeers < 0 || npeers > b200::kMaxPeers || (npeers > 0 && peer_d == nullptr)) {
+        b200::set_error("set_peers: plan must be valid and npeers in [0, %d]", b200::kMaxPeers);
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    for (int g = 0; g < npeers; ++g) {
+        if (peer_d[g] == nullptr || reinterpret_cast<uintptr_t>(peer_d[g]) % 16 != 0) {
+            b200::set_error("set_peers: peer pointer %d is NULL or not 16-byte aligned", g);
+            return B200_ERR_INVALID_ARGUMENT;
+        }
+    }
+    plan->params.npeers = npeers;
+    plan->params.ldd = plan->info.ldd;
+    for (int g = 0; g < b200::kMaxPeers; ++g) plan->params.peer_d[g] = g < npeers ? peer_d[g] : nullptr;
+    return B200_OK;
 }
 
 int b200_gemm_plan_set_trace(B200Plan* plan, unsigned long long* trace, int64_t slots_per_cta) {

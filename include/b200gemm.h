@@ -192,6 +192,25 @@ int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, voi
 int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
                       int64_t ldd, int out_dtype, int mode, void* stream);
 
+/* Fused gather for the N-sharded multi-GPU GEMM. After set_peers, every launch
+ * also writes each output chunk into the npeers (<= 7) peer buffers with
+ * 16-byte stores over NVLink, at the same rows/columns and row pitch as the
+ * plan's own D; peer_d[g] must already point at this shard's first column in
+ * peer g's full matrix (see b200_peer_*). The caller orders the ranks after
+ * the launch (e.g. one NCCL all-reduce of a scalar) before reading peers'
+ * data. npeers = 0 turns it off. No counterpart in the reference (no
+ * multi-GPU path there); replaces GEMM-then-all-gather with one kernel. */
+int b200_gemm_plan_set_peers(B200Plan* plan, int npeers, void* const* peer_d);
+
+/* Peer-visible buffers (CUDA IPC) for the fused gather. alloc: cudaMalloc of
+ * `bytes` plus its IPC handle (b200_ipc_handle_size() bytes written to
+ * out_handle); open/close map another process's buffer on the current device. */
+size_t b200_ipc_handle_size(void);
+int b200_peer_buffer_alloc(int64_t bytes, void** out_ptr, void* out_handle);
+int b200_peer_buffer_free(void* ptr);
+int b200_peer_open(const void* handle, void** out_ptr);
+int b200_peer_close(void* ptr);
+
 /* Timeline tracing (off by default). trace: device buffer of grid_ctas x 64
  * uint64 (%globaltimer ns) that each later execute fills per CTA: [0] entry,
  * [1] setup done, [2] producer done, [3] MMA issuer done, [4] epilogue done,

@@ -1,7 +1,9 @@
-"""N-sharded GEMM over NCCL on every visible GPU (skipped with fewer than 2).
+"""N-sharded GEMM on every visible GPU (skipped with fewer than 2).
 
 Each rank runs the B200 kernel on its output columns; the full matrix is
-gathered with one NCCL all-gather and compared with the CPU oracle.
+gathered either with one NCCL all-gather or by the kernel itself (fused
+gather: peer stores over NVLink), and compared on every rank with the CPU
+oracle. NVLS is off (NCCL_NVLS_ENABLE=0) and no multicast object is used.
 """
 import os
 import socket
@@ -38,13 +40,18 @@ def _worker(rank, world, port, q):
         m, n, k = 384, 1000, 256
         a, b = operands.uniform_operands(m, n, k, seed=12)
         n0, n1 = bdist.shard_bounds(n, world, rank)
-        sg = bdist.ShardedGemm(a.to(dev), b[n0:n1].contiguous().to(dev), n)
-        full = sg.run("full")
-        sg.synchronize()
-        torch.cuda.synchronize()
         ref = torch.from_numpy(oracle.gemm_tn_f64(a, b))
-        check.bf16_tolerance_check(f"rank {rank}", ref, full.cpu(), k, 1.0, 1.0)
-        sg.destroy()
+        for p2p in (False, True):
+            for mode in ("2cta", "2cta_m512", "1cta"):
+                sg = bdist.ShardedGemm(a.to(dev), b[n0:n1].contiguous().to(dev), n, mode=mode,
+                                       p2p=p2p)
+                for _ in range(2):  # twice: the second launch reuses the plan and buffers
+                    full = sg.run("full")
+                    sg.synchronize()
+                    torch.cuda.synchronize()
+                    check.bf16_tolerance_check(f"rank {rank} p2p={p2p} {mode}", ref, full.cpu(), k,
+                                               1.0, 1.0)
+                sg.destroy()
         q.put((rank, True, ""))
     except Exception as exc:
         q.put((rank, False, repr(exc)))
