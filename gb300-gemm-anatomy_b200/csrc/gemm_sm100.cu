@@ -401,6 +401,12 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 const uint32_t t_row = tmem_base + slot * kBN + (static_cast<uint32_t>(q * 32) << 16);
                 // Stage one 32-row x 128-byte chunk of this warp's rows and TMA-store it.
                 auto store_chunk = [&](int c, const uint32_t* packed) {
+                    // Chunks wholly outside D are skipped before touching the staging
+                    // buffers: every staged chunk must commit one bulk group, or the
+                    // wait_group.read accounting below would let a later chunk overwrite
+                    // a buffer whose store is still reading it.
+                    const int col = col0 + c * kColsPerChunk;
+                    if (row0 >= p.m || col >= p.n) return;
                     const uint32_t sbuf = stage_buf0 + buf * kEpiBufBytes;
                     if (lane == 0) bulk_wait_group_read<1>();
                     __syncwarp();
@@ -412,12 +418,11 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
-                    const int col = col0 + c * kColsPerChunk;
-                    if (lane == 0 && row0 < p.m && col < p.n) {
+                    if (lane == 0) {
                         tma_store_2d(&tmD, sbuf, col, row0);
                         bulk_commit_group();
                     }
-                    if (p.npeers > 0 && row0 < p.m && col < p.n) {
+                    if (p.npeers > 0) {
                         // Fused gather: 8 lanes cover one 128-byte staged row, so each
                         // warp store writes four contiguous 128-byte row segments.
                         constexpr int kElem = 128 / kColsPerChunk;

@@ -64,7 +64,8 @@ def test_c1_512(golden_dir, mode):
 
 
 @pytest.mark.parametrize("shape", [(1, 8, 8), (17, 24, 8), (129, 264, 72), (300, 1000, 520),
-                                   (640, 136, 4104), (1000, 16, 64), (1100, 520, 200)])
+                                   (640, 136, 4104), (1000, 16, 64), (1100, 520, 200),
+                                   (384, 104, 256), (384, 128, 64), (2048, 64, 512)])
 @pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512"])
 def test_ragged_shapes(shape, mode):
     m, n, k = shape
@@ -151,3 +152,20 @@ def test_unaligned_pitch_rejected():
     assert not ok and "16 bytes" in why
     ok, _ = G.supported(64, 257, 64, out_dtype=torch.float32, ldd=260)
     assert ok
+
+
+@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512"])
+@pytest.mark.parametrize("n", [16, 64, 104, 128, 192])
+def test_narrow_n_strided_repeat(mode, n):
+    """Output narrower than one 256-column tile (some 64-column chunks fall
+    outside D), placed in a wider zeroed buffer, five launches in a row: every
+    element of D is written every time and nothing outside it."""
+    m, k, ld = 384, 256, 256
+    a, b = operands.uniform_operands(m, n, k, seed=6)
+    ref = torch.from_numpy(oracle.gemm_tn_f64(a, b))
+    for _ in range(5):
+        big = torch.zeros((m, ld), dtype=torch.bfloat16, device=DEV)
+        G.gemm(a.to(DEV), b.to(DEV), big[:, :n], mode=mode)
+        host = big.cpu()
+        check.bf16_tolerance_check(f"narrow {n}/{mode}", ref, host[:, :n], k, maxabs(a), maxabs(b))
+        assert bool((host[:, n:] == 0).all())
