@@ -7,7 +7,8 @@ its shard. For each shape it checks the gathered D against a torch fp32
 reference on sampled rows, then times (CUDA events, max over ranks):
   none   the sharded GEMM alone (weak scaling of the compute)
   nccl   GEMM, then NCCL all-gather of the bf16 shards and the re-layout
-  p2p    the fused gather: the GEMM epilogue writes every tile to every peer
+  p2p    the fused gather: the GEMM epilogue TMA-stores every tile to every peer
+  p2p_st the fused gather with per-thread 16-byte stores instead of TMA
 Prints one CSV row per (shape, gather) on rank 0.
 """
 from __future__ import annotations
@@ -25,7 +26,7 @@ def main(argv=None) -> int:
     ap.add_argument("--shape", action="append", help="NxK (repeatable); default: the LLM shapes")
     ap.add_argument("--iterations", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--gathers", default="none,nccl,p2p")
+    ap.add_argument("--gathers", default="none,nccl,p2p,p2p_st")
     args = ap.parse_args(argv)
     import torch
     import torch.distributed as dist
@@ -48,7 +49,12 @@ def main(argv=None) -> int:
         idx = torch.arange(0, args.m, max(args.m // 64, 1))
         ref = a_h[idx].float() @ b_h.float().T
         for gather in args.gathers.split(","):
-            sg = bdist.ShardedGemm(a, b, n, p2p=(gather == "p2p"))
+            # p2p: fused gather with TMA bulk stores to the peers; p2p_st: 16-byte stores.
+            if gather == "p2p_st":
+                os.environ["B200_PEER_STORES"] = "st"
+            else:
+                os.environ.pop("B200_PEER_STORES", None)
+            sg = bdist.ShardedGemm(a, b, n, p2p=gather.startswith("p2p"))
             mode = "none" if gather == "none" else "full"
             full = sg.run(mode)
             torch.cuda.synchronize()

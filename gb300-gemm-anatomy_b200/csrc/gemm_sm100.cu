@@ -93,8 +93,14 @@ struct GemmParams {
     // the same row/column (peer_d already points at this shard's columns;
     // the same row pitch as the local D). npeers = 0: off.
     int npeers;
+    int peer_tma;    // 1: peer chunks go out as TMA bulk stores (PeerMaps), 0: 16-byte stores
     long long ldd;
     void* peer_d[kMaxPeers];
+};
+
+// Tensor maps of the peers' D slices for the TMA form of the fused gather.
+struct PeerMaps {
+    CUtensorMap map[kMaxPeers];
 };
 
 // Trace slots per CTA: 0 entry, 1 setup done, 2 producer done, 3 MMA done,
@@ -126,7 +132,8 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mb,
 template <int kCtaGroup, int kSubM, bool kOutF32>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmD, const GemmParams p,
+                     const __grid_constant__ PeerMaps peers) {
     using C = GemmCfg<kCtaGroup, kSubM>;
     constexpr int kStages = C::kStages;
     constexpr int kColsPerChunk = kOutF32 ? 32 : 64;  // output columns per 128-byte staging row
@@ -420,9 +427,13 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     __syncwarp();
                     if (lane == 0) {
                         tma_store_2d(&tmD, sbuf, col, row0);
+                        if (p.peer_tma) {
+                            // Same staged box to every peer's D: one bulk group per chunk.
+                            for (int g = 0; g < p.npeers; ++g) tma_store_2d(&peers.map[g], sbuf, col, row0);
+                        }
                         bulk_commit_group();
                     }
-                    if (p.npeers > 0) {
+                    if (p.npeers > 0 && !p.peer_tma) {
                         // Fused gather: 8 lanes cover one 128-byte staged row, so each
                         // warp store writes four contiguous 128-byte row segments.
                         constexpr int kElem = 128 / kColsPerChunk;
@@ -500,7 +511,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmParams);
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmParams, PeerMaps);
 
 // Kernel variants: (cta_group, sub_m) in {(1,1), (2,1), (2,2)} x {bf16, fp32} D.
 template <int G, int S>
@@ -533,6 +544,7 @@ struct B200Plan {
     int sub_m = 1;  // 128-row accumulators per CTA per tile
     bool out_f32 = false;
     CUtensorMap tmA{}, tmB{}, tmD{};
+    b200::PeerMaps peer_maps{};
     b200::GemmParams params{};
     int grid = 0;
     int smem = 0;
@@ -813,7 +825,8 @@ static int plan_launch(B200Plan* plan, cudaStream_t stream) {
     }
     cudaError_t err;
 #define B200_LAUNCH(G, S, F) \
-    cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<G, S, F>, plan->tmA, plan->tmB, plan->tmD, plan->params)
+    cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<G, S, F>, plan->tmA, plan->tmB, plan->tmD, plan->params, \
+                       plan->peer_maps)
     if (plan->cta_group == 1)
         err = plan->out_f32 ? B200_LAUNCH(1, 1, true) : B200_LAUNCH(1, 1, false);
     else if (plan->sub_m == 2)
@@ -924,7 +937,21 @@ int b200_gemm_plan_set_peers(B200Plan* plan, int npeers, void* const* peer_d) {
             return B200_ERR_INVALID_ARGUMENT;
         }
     }
+    // Peer chunks go out as TMA bulk stores by default (one per peer per staged
+    // chunk); B200_PEER_STORES=st selects per-thread 16-byte stores instead.
+    int use_tma = 1;
+    if (const char* e = std::getenv("B200_PEER_STORES")) use_tma = !(e[0] == 's' && e[1] == 't');
+    const b200::GemmParams& q = plan->params;
+    for (int g = 0; g < npeers && use_tma; ++g) {
+        const int rc = plan->out_f32
+            ? b200::encode_tmap_2d(&plan->peer_maps.map[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, peer_d[g],
+                                   q.m, q.n, plan->info.ldd, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B)
+            : b200::encode_tmap_2d(&plan->peer_maps.map[g], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, peer_d[g],
+                                   q.m, q.n, plan->info.ldd, 32, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc != B200_OK) return rc;
+    }
     plan->params.npeers = npeers;
+    plan->params.peer_tma = use_tma;
     plan->params.ldd = plan->info.ldd;
     for (int g = 0; g < b200::kMaxPeers; ++g) plan->params.peer_d[g] = g < npeers ? peer_d[g] : nullptr;
     return B200_OK;

@@ -41,7 +41,11 @@ def _worker(rank, world, port, q):
         a, b = operands.uniform_operands(m, n, k, seed=12)
         n0, n1 = bdist.shard_bounds(n, world, rank)
         ref = torch.from_numpy(oracle.gemm_tn_f64(a, b))
-        for p2p in (False, True):
+        for p2p, stores in ((False, None), (True, "tma"), (True, "st")):
+            if stores == "st":
+                os.environ["B200_PEER_STORES"] = "st"
+            else:
+                os.environ.pop("B200_PEER_STORES", None)
             for mode in ("2cta", "2cta_m512", "1cta"):
                 sg = bdist.ShardedGemm(a.to(dev), b[n0:n1].contiguous().to(dev), n, mode=mode,
                                        p2p=p2p)
