@@ -57,3 +57,34 @@ def test_memory_paths_grids():
     assert sorted({g[2] * g[1] // 1024 for g in ref}) == [16, 32, 64]
     base = mp.baseline_grid()
     assert {g[3] for g in base} == {1, 2, 4} and {g[2] for g in base} == {16384}
+
+
+FAKE_NCU_CSV = '''==PROF== Connected to process
+"ID","Process ID","Process Name","Host Name","Kernel Name","Context","Stream","Block Size","Grid Size","Device","CC","Section Name","Metric Name","Metric Unit","Metric Value"
+"0","1","python","h","ldgsts_stream_kernel","1","7","(128, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","dram__bytes_read.sum","byte","1,073,825,792"
+"0","1","python","h","ldgsts_stream_kernel","1","7","(128, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","gpu__time_duration.sum","us","157.70"
+"0","1","python","h","ldgsts_stream_kernel","1","7","(128, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","sm__cycles_elapsed.avg.per_second","Ghz","1.50"
+'''
+
+
+def test_ncu_bridge_parsing_and_classification():
+    sys.path.insert(0, ENV_PATH)
+    from b200gemm.cli import ncu_bridge as nb
+    m = nb.parse_csv(FAKE_NCU_CSV)
+    assert m["dram__bytes_read.sum"] == 1073825792
+    assert abs(m["gpu__time_duration.sum"] - 157.7e-6) < 1e-12
+    r = nb.summarise("memory", m, useful_bytes=1 << 30)
+    assert r["classification"] == "HBM_VALIDATED" and r["flags"] == []
+    assert abs(r["effective_gbps"] - (1 << 30) / 157.7e-6 / 1e9) < 1e-6
+    r = nb.summarise("memory", m, useful_bytes=(1 << 30) * 2)
+    assert r["classification"] == "INCONCLUSIVE"
+    t = nb.summarise("tensor", m, flop=2 * 8192 ** 3)
+    assert abs(t["sm_clock_ghz"] - 1.5) < 1e-9
+    cmd = nb.ncu_command("memory", "ldgsts", 1, ["python", "x.py"])
+    assert cmd[:3] == ["ncu", "--clock-control", "none"] and "--launch-count" in cmd
+
+
+def test_ncu_bridge_usage():
+    assert run("b200gemm.cli.ncu_bridge", "--kind", "memory").returncode == 2
+    r = run("b200gemm.cli.ncu_bridge", "--kind", "memory", "--kernel", "x", "--", "true")
+    assert r.returncode == 2  # memory kind needs --useful-bytes
