@@ -197,6 +197,11 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
     if constexpr (kPair) cluster_sync(); else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+    // Everything above touched only shared memory, TMEM and the kernel
+    // parameters, so with programmatic dependent launch it overlaps the tail of
+    // the previous kernel in the stream; no global memory (operands, D, the tile
+    // counter, the status word) is touched before this wait.
+    griddep_wait();
     if (threadIdx.x == 0) trace_stamp(p, 1);
 
     // Tile-id queue. The leader's producer fetches ids from the global counter
@@ -216,8 +221,8 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         if (elect_one()) {
             uint32_t stage = 0, phase = 0, qs = 0, qph = 0;
             bool ok = true;
-            // The leader fetches tile ids one tile ahead so the atomic's round
-            // trip overlaps the current tile's loads instead of delaying the next.
+            // The leader fetches the first tile id now and each later one while the
+            // current tile is still loading (see fetch_kb).
             int next = (rank == 0) ? atomicAdd(&p.tile_counter[0], 1) : -1;
             while (ok) {
                 int t;
@@ -236,8 +241,6 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                             atomicExch(&p.tile_counter[0], 0);
                             atomicExch(&p.tile_counter[1], 0);
                         }
-                    } else {
-                        next = atomicAdd(&p.tile_counter[0], 1);
                     }
                     ring[qs] = t;
                     if constexpr (kPair) {
@@ -251,12 +254,22 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     queue_release(qs);
                 }
                 if (++qs == kQueue) { qs = 0; qph ^= 1; }
-                if (t < 0) break;
+                if (t < 0) {
+                    // No more tiles for this CTA: the next launch may start its setup.
+                    griddep_launch_dependents();
+                    break;
+                }
                 int mb, nb;
                 tile_coords(t, p, mb, nb);
                 const int a_row = mb * C::kTileM + static_cast<int>(rank) * C::kARows;
                 const int b_row = nb * kBN + static_cast<int>(rank) * C::kBRows;
+                // The next tile id is fetched late in this tile (two ring depths
+                // before its last k-slice): early enough to hide the atomic's round
+                // trip, late enough that a fast pair cannot take two tiles while a
+                // slow one has none.
+                const int fetch_kb = max(0, p.num_k_blocks - 2 * kStages);
                 for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (rank == 0 && kb == fetch_kb) next = atomicAdd(&p.tile_counter[0], 1);
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.status, p.timeout_ns,
                                    B200_DEV_TIMEOUT_PRODUCER)) {
                         ok = false;
@@ -542,6 +555,7 @@ struct B200Plan {
     cudaStream_t stream = nullptr;
     int cta_group = 1;
     int sub_m = 1;  // 128-row accumulators per CTA per tile
+    bool pdl = false;  // launch with programmatic stream serialization
     bool out_f32 = false;
     CUtensorMap tmA{}, tmB{}, tmD{};
     b200::PeerMaps peer_maps{};
@@ -693,6 +707,9 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
     plan->cta_group = resolved == B200_MODE_1CTA ? 1 : 2;
     plan->sub_m = resolved == B200_MODE_2CTA_M512 ? 2 : 1;
     plan->empty_problem = empty;
+    // Programmatic dependent launch: on unless B200_PDL=0.
+    plan->pdl = true;
+    if (const char* e = std::getenv("B200_PDL")) plan->pdl = e[0] != '0';
 
     const int tile_m = kRowsPerCta * plan->sub_m * plan->cta_group;
     GemmParams& p = plan->params;
@@ -810,18 +827,24 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
 static int plan_launch(B200Plan* plan, cudaStream_t stream) {
     if (plan->empty_problem) return B200_OK;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(plan->grid, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = plan->smem;
     cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 0;
     if (plan->cta_group == 2) {
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        attr[cfg.numAttrs].val.clusterDim.x = 2;
+        attr[cfg.numAttrs].val.clusterDim.y = 1;
+        attr[cfg.numAttrs].val.clusterDim.z = 1;
+        ++cfg.numAttrs;
+    }
+    if (plan->pdl) {
+        attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+        ++cfg.numAttrs;
     }
     cudaError_t err;
 #define B200_LAUNCH(G, S, F) \

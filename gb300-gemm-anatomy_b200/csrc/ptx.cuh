@@ -64,6 +64,17 @@ __device__ __forceinline__ void cluster_sync() {
                  "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// Programmatic dependent launch. wait: block until every prerequisite grid
+// has completed and its memory is visible (a no-op when the launch did not
+// opt in). launch_dependents: this CTA no longer holds back the next launch.
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Records a failure in the launch's device status word (first code wins).
 __device__ __forceinline__ void report_status(int* status, int code) {
     if (status != nullptr) atomicCAS(status, 0, code);
