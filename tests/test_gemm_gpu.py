@@ -169,3 +169,27 @@ def test_narrow_n_strided_repeat(mode, n):
         host = big.cpu()
         check.bf16_tolerance_check(f"narrow {n}/{mode}", ref, host[:, :n], k, maxabs(a), maxabs(b))
         assert bool((host[:, n:] == 0).all())
+
+
+@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512"])
+def test_launch_after_producer_kernel_sees_its_writes(mode):
+    """Plans launch with programmatic dependent launch: a GEMM that follows a
+    kernel writing its operand must still read the new values (no global access
+    before griddepcontrol.wait), launch after launch on one stream."""
+    m, n, k = 1024, 768, 512
+    a, b = operands.uniform_operands(m, n, k, seed=7)
+    a_d, b_d = a.to(DEV), b.to(DEV)
+    outs = [torch.empty((m, n), dtype=torch.float32, device=DEV) for _ in range(6)]
+    plans = [G.GemmPlan(a_d, b_d, o, mode=mode) for o in outs]
+    for i, plan in enumerate(plans):
+        a_d.mul_(-1.0 if i % 2 == 0 else 2.0)  # an elementwise kernel right before the GEMM
+        plan.execute()
+    for plan in plans:
+        plan.synchronize()
+        plan.destroy()
+    ref = a.double() @ b.double().T
+    scale = 1.0
+    for i, o in enumerate(outs):
+        scale *= -1.0 if i % 2 == 0 else 2.0
+        err = float((o.cpu().double() - scale * ref).abs().max())
+        assert err <= 1e-2 * abs(scale), (i, err)
