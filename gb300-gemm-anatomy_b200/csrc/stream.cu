@@ -12,9 +12,9 @@
 //  * LDGSTS: every thread only ever reads back the 16-byte vectors it copied
 //    itself, so the ring needs no __syncthreads at all (the reference pays two
 //    per tile); cp.async.wait_group alone orders copy and use.
-//  * TMA: a dedicated leader refills a slot as soon as the four consumer warps
-//    have released it (empty mbarrier, one arrival per warp), and a second
-//    geometry uses the GEMM's 128-byte-swizzled 64-element rows.
+//  * TMA: four independent per-warp pipelines (each warp loads and reads its
+//    own quarter of every stage), and a second geometry uses the GEMM's
+//    128-byte-swizzled 64-element rows.
 //  * CTAs/SM in {1, 2, 4} with an occupancy-checked shared-memory reservation,
 //    tile ranges balanced across the grid so any multiple of stage_bytes works
 //    (4 GiB included), and a full-buffer XOR/sum checksum mode that is
@@ -203,8 +203,11 @@ ldgsts_stream_kernel(const StreamParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA ring. Thread 0 issues; every warp releases a slot with one arrival on
-// its empty barrier after reading it.
+// TMA ring, one independent pipeline per warp: warp w owns the w-th quarter of
+// every stage, its lane 0 issues that quarter's boxes on the warp's own full
+// barrier and refills it as soon as the warp has read it, so no warp ever
+// waits for another (the refill in a CTA-wide ring waits for the slowest warp
+// every step, which halved the throughput at small stages).
 // ---------------------------------------------------------------------------
 template <int STAGES>
 __global__ void __launch_bounds__(kStreamThreads)
@@ -212,79 +215,70 @@ tma_stream_kernel(const __grid_constant__ CUtensorMap tmap, const StreamParams p
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
-    const int tid = threadIdx.x, lane = tid & 31;
+    constexpr int kWarps = kStreamThreads / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + static_cast<uint32_t>(STAGES * p.stage_bytes);
-    const uint32_t full0 = bar0, empty0 = bar0 + 8 * STAGES;
+    const uint32_t full_w = bar0 + 8 * STAGES * warp;  // this warp's STAGES barriers
     int64_t tile0, ntiles;
     tile_range(p, tile0, ntiles);
     const int64_t total_steps = ntiles * p.passes;
-    const int vecs = static_cast<int>(p.stage_bytes / 16);
+    const int qbytes = static_cast<int>(p.stage_bytes / kWarps);
+    const int qvecs = qbytes / 16;
+    const int rows_per_tile = static_cast<int>(p.stage_bytes / p.row_bytes);
+    const int qrows = rows_per_tile / kWarps;
 
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, kStreamThreads / 32);
-        }
+        for (int i = 0; i < kWarps * STAGES; ++i) mbar_init(bar0 + 8 * i, 1);
         fence_barrier_init();
         tma_prefetch_desc(&tmap);
     }
     __syncthreads();
 
     TileWalk issue_walk(tile0, ntiles, p.rotation), use_walk(tile0, ntiles, p.rotation);
-    const int rows_per_tile = p.box_rows * p.boxes_per_stage;
-    auto issue = [&](int64_t step) {
+    auto issue = [&](int64_t step) {  // lane 0 only
         const int s = static_cast<int>(step % STAGES);
-        const uint32_t slot = sbase + static_cast<uint32_t>(s * p.stage_bytes);
-        const int64_t row = issue_walk.tile() * rows_per_tile;
+        const uint32_t slot = sbase + static_cast<uint32_t>(s * p.stage_bytes + warp * qbytes);
+        const int64_t row = issue_walk.tile() * rows_per_tile + warp * qrows;
         issue_walk.next();
-        mbar_arrive_expect_tx(full0 + 8 * s, static_cast<uint32_t>(p.stage_bytes));
+        mbar_arrive_expect_tx(full_w + 8 * s, static_cast<uint32_t>(qbytes));
         for (int b = 0; b < p.boxes_per_stage; ++b)
-            tma_load_2d(slot + b * p.box_rows * p.row_bytes, &tmap, full0 + 8 * s, 0,
+            tma_load_2d(slot + b * p.box_rows * p.row_bytes, &tmap, full_w + 8 * s, 0,
                         static_cast<int32_t>(row + b * p.box_rows));
     };
 
     Consumer cons;
-    bool ok = true;
-    if (tid == 0) {
+    if (lane == 0) {
         for (int64_t s = 0; s < STAGES && s < total_steps; ++s) issue(s);
     }
-    for (int64_t step = 0; ok && step < total_steps; ++step) {
+    for (int64_t step = 0; step < total_steps; ++step) {
         const int s = static_cast<int>(step % STAGES);
         const uint32_t parity = static_cast<uint32_t>((step / STAGES) & 1);
-        if (!mbar_wait(full0 + 8 * s, parity, &p.counters->status, p.timeout_ns,
+        if (!mbar_wait(full_w + 8 * s, parity, &p.counters->status, p.timeout_ns,
                        B200_DEV_TIMEOUT_STREAM)) {
-            ok = false;
             break;
         }
-        const uint8_t* slot = smem + s * p.stage_bytes;
+        const uint8_t* slot = smem + s * p.stage_bytes + warp * qbytes;
         const int64_t tile = use_walk.tile();
         use_walk.next();
         if (p.mode == B200_STREAM_SINK) {
-            cons.sink ^= *reinterpret_cast<const uint32_t*>(slot + tid * 16);
+            cons.sink ^= *reinterpret_cast<const uint32_t*>(slot + lane * 16);
         } else {
-            const uint64_t vec0 = static_cast<uint64_t>(tile * (p.stage_bytes / 16));
-            for (int v = tid; v < vecs; v += kStreamThreads) {
+            const uint64_t vec0 = static_cast<uint64_t>(tile * (p.stage_bytes / 16) + warp * qvecs);
+            for (int v = lane; v < qvecs; v += 32) {
                 const uint4 x = *reinterpret_cast<const uint4*>(slot + v * 16);
                 uint64_t logical = static_cast<uint64_t>(v);
                 if (p.swizzled) {
-                    // 128-byte rows; the 16-byte chunk c of row r sits at c ^ (r % 8).
+                    // 128-byte rows from a 1024-byte aligned quarter; the 16-byte
+                    // chunk c of row r sits at c ^ (r % 8).
                     const int r = v >> 3, c = v & 7;
                     logical = static_cast<uint64_t>(r * 8 + (c ^ (r & 7)));
                 }
                 cons.vector(p.mode, x, vec0 + logical);
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty0 + 8 * s);
-        if (tid == 0 && step + STAGES < total_steps) {
-            if (!mbar_wait(empty0 + 8 * s, parity, &p.counters->status, p.timeout_ns,
-                           B200_DEV_TIMEOUT_STREAM)) {
-                ok = false;
-                break;
-            }
-            issue(step + STAGES);
-        }
+        __syncwarp();  // the whole warp has read its quarter
+        if (lane == 0 && step + STAGES < total_steps) issue(step + STAGES);
     }
     cons.flush(p);
     __syncthreads();
@@ -323,6 +317,11 @@ static int check_stream_config(const B200StreamConfig* c) {
     if (c->stage_bytes < 2048 || c->stage_bytes > 65536 || c->stage_bytes % 2048 != 0) {
         set_error("stage_bytes=%lld must be a multiple of 2048 in [2048, 65536]",
                   (long long)c->stage_bytes);
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (c->method == B200_STREAM_TMA_SW128 && c->stage_bytes % 4096 != 0) {
+        set_error("TMA_SW128 needs stage_bytes %% 4096 == 0 (each warp's quarter of a stage "
+                  "must hold whole 1024-byte swizzle atoms), got %lld", (long long)c->stage_bytes);
         return B200_ERR_INVALID_ARGUMENT;
     }
     if (c->ctas_per_sm != 1 && c->ctas_per_sm != 2 && c->ctas_per_sm != 4) {
@@ -410,7 +409,7 @@ int b200_stream_plan_create(const B200StreamConfig* cfg, const void* buf, int64_
 
     const bool tma = cfg->method != B200_STREAM_LDGSTS;
     const int64_t payload = cfg->stages * cfg->stage_bytes;
-    const int64_t need = payload + (tma ? 1024 + 16 * cfg->stages : 0);
+    const int64_t need = payload + (tma ? 1024 + 8 * 4 * cfg->stages : 0);
     // Reserve enough that no more than ctas_per_sm CTAs fit on one SM (the
     // reference forces exactly one with the same device, ldgsts.cu:806-843).
     const int64_t per_sm = props.smem_per_sm;
@@ -455,9 +454,10 @@ int b200_stream_plan_create(const B200StreamConfig* cfg, const void* buf, int64_
         const bool sw = cfg->method == B200_STREAM_TMA_SW128;
         p.row_bytes = sw ? 128 : 256;
         p.swizzled = sw ? 1 : 0;
-        const int rows = static_cast<int>(cfg->stage_bytes / p.row_bytes);
-        p.box_rows = std::min(rows, 256);
-        p.boxes_per_stage = rows / p.box_rows;
+        // Each of the 4 warps loads a quarter of a stage (see tma_stream_kernel).
+        const int qrows = static_cast<int>(cfg->stage_bytes / p.row_bytes) / 4;
+        p.box_rows = std::min(qrows, 256);
+        p.boxes_per_stage = qrows / p.box_rows;
         const uint64_t total_rows = static_cast<uint64_t>(bytes / p.row_bytes);
         rc = b200::encode_tmap_2d(&plan->tmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, buf, total_rows,
                                   p.row_bytes / 2, p.row_bytes / 2, p.box_rows, p.row_bytes / 2,

@@ -42,6 +42,11 @@ def test_reference_grid_validate(pattern_buf, method, stages, bif_kib):
     sb = mp.stage_bytes_for(bif_kib, stages)
     nbytes = (pattern_buf.numel() * 2 // sb) * sb
     buf = pattern_buf[: nbytes // 2]
+    if method == "tma_sw128" and sb % 4096:
+        # each warp's quarter of a swizzled stage must hold whole 1024-byte atoms
+        with pytest.raises(mp._lib.BridgeError):
+            mp.StreamPlan(buf, method, stages, sb)
+        return
     plan = mp.StreamPlan(buf, method, stages, sb, ctas_per_sm=1, passes=2, rotation=3)
     plan.execute("validate")
     r = plan.result()
@@ -94,3 +99,22 @@ def test_invalid_configs(pattern_buf):
         mp.StreamPlan(pattern_buf, "ldgsts", 3, 8192)
     with pytest.raises(mp._lib.BridgeError):
         mp.StreamPlan(pattern_buf, "ldgsts", 8, 65536, ctas_per_sm=4)
+
+
+@pytest.mark.parametrize("method", ["tma", "tma_sw128"])
+def test_tma_sink_matches_host(pattern_buf, method):
+    """TMA SINK: warp w, lane l reads word 0 of vector l of quarter w of each stage."""
+    sb = 8192
+    nbytes = sm_count() * 4 * sb
+    buf = pattern_buf[: nbytes // 2]
+    plan = mp.StreamPlan(buf, method, 4, sb, ctas_per_sm=1, passes=1)
+    plan.execute("sink")
+    r = plan.result()
+    plan.destroy()
+    w = buf.view(torch.int32).cpu().numpy().view(np.uint32).reshape(-1, 4, sb // 64, 4)
+    # quarter q, 16-byte slot l (l < 32) in shared memory; with the 128-byte swizzle
+    # slot l holds vector (l >> 3) * 8 + ((l & 7) ^ ((l >> 3) & 7)) of the quarter
+    lanes = np.arange(32)
+    vec = lanes if method == "tma" else (lanes >> 3) * 8 + ((lanes & 7) ^ ((lanes >> 3) & 7))
+    expect = int(np.bitwise_xor.reduce(w[:, :, vec, 0].reshape(-1)))
+    assert r["sink_xor"] == expect
