@@ -45,6 +45,9 @@ CANDIDATES = (
      "cluster": (2, 1), "use_2cta_instrs": True},
     {"method": "b200", "variant": "persistent_2cta_m512", "mode": "2cta_m512",
      "mma_tiler": (512, 256), "cluster": (2, 1), "use_2cta_instrs": True},
+    # The library's own choice per shape (B200_MODE_AUTO).
+    {"method": "b200", "variant": "persistent_auto", "mode": "auto", "mma_tiler": None,
+     "cluster": None, "use_2cta_instrs": None},
     {"method": "cublas", "variant": "torch_matmul", "mode": None, "mma_tiler": None,
      "cluster": None, "use_2cta_instrs": None},
     # The reference's own cuBLASLt bridge (cublaslt_bridge_p35.cu), built unmodified by
@@ -111,8 +114,9 @@ def build_arg_parser() -> argparse.ArgumentParser:
                    help="explicit MxNxK (repeatable); overrides --shapes")
     p.add_argument("--operands", choices=("ref-compat", "config"), default="ref-compat")
     p.add_argument("--out-dtype", choices=("f32", "bf16"), default="f32")
-    p.add_argument("--candidates", default="persistent_1cta,persistent_2cta,torch_matmul",
-                   help="comma list of persistent_1cta, persistent_2cta, persistent_2cta_m512, "
+    p.add_argument("--candidates", default="persistent_auto,torch_matmul",
+                   help="comma list of persistent_auto, persistent_1cta, persistent_2cta, "
+                        "persistent_2cta_m512, "
                         "torch_matmul, "
                         "heuristic_first_supported (the reference's cuBLASLt bridge)")
     p.add_argument("--peak-tflops", type=float, default=None,

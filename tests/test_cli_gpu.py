@@ -21,7 +21,8 @@ def run(mod, *args, timeout=600):
 
 def test_gemm_comparison_ref_compat_exact():
     r = run("b200gemm.cli.gemm_comparison", "--shape", "512x512x512", "--shape", "256x1024x768",
-            "--iterations", "3", "--warmup-iterations", "1")
+            "--iterations", "3", "--warmup-iterations", "1",
+            "--candidates", "persistent_1cta,persistent_2cta,torch_matmul")
     assert r.returncode == 0, r.stderr
     rows = list(csv.DictReader(io.StringIO(r.stdout)))
     assert len(rows) == 6
