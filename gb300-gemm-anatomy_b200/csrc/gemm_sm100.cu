@@ -220,6 +220,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         // ------------------------------------------------------------ producer
         if (elect_one()) {
             uint32_t stage = 0, phase = 0, qs = 0, qph = 0;
+            long long issued = 0;  // ring slots armed so far (failure-path drain)
             bool ok = true;
             // The leader fetches the first tile id now and each later one while the
             // current tile is still loading (see fetch_kb).
@@ -288,7 +289,19 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         tma_load_2d_pair(sa, &tmA, leader_fb, kb * kBK, a_row);
                         tma_load_2d_pair(sb, &tmB, leader_fb, kb * kBK, b_row);
                     }
+                    ++issued;
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+            }
+            if (status_failed(p.status) && rank == 0) {
+                // The launch is being abandoned: before this CTA (pair) exits, wait
+                // (bounded) for the TMA loads it still has in flight into its ring.
+                const unsigned long long drain_ns = min(p.timeout_ns, 100000000ull);
+                for (int s = 0; s < kStages; ++s) {
+                    if (issued <= s) continue;
+                    const long long last = ((issued - 1 - s) / kStages) * kStages + s;
+                    mbar_wait(full0 + 8 * s, static_cast<uint32_t>((last / kStages) & 1), nullptr,
+                              drain_ns, 0);
                 }
             }
             trace_stamp(p, 2);

@@ -256,6 +256,13 @@ tma_stream_kernel(const __grid_constant__ CUtensorMap tmap, const StreamParams p
         const uint32_t parity = static_cast<uint32_t>((step / STAGES) & 1);
         if (!mbar_wait(full_w + 8 * s, parity, &p.counters->status, p.timeout_ns,
                        B200_DEV_TIMEOUT_STREAM)) {
+            // Abandoning: wait (bounded) for this warp's loads still in flight.
+            if (lane == 0) {
+                const unsigned long long drain_ns = min(p.timeout_ns, 100000000ull);
+                for (int64_t q = step; q < step + STAGES && q < total_steps; ++q)
+                    mbar_wait(full_w + 8 * static_cast<int>(q % STAGES),
+                              static_cast<uint32_t>((q / STAGES) & 1), nullptr, drain_ns, 0);
+            }
             break;
         }
         const uint8_t* slot = smem + s * p.stage_bytes + warp * qbytes;
