@@ -455,7 +455,13 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         tma_store_2d(&tmD, sbuf, col, row0);
                         if (p.peer_tma) {
                             // Same staged box to every peer's D: one bulk group per chunk.
-                            for (int g = 0; g < p.npeers; ++g) tma_store_2d(&peers.map[g], sbuf, col, row0);
+                            // Rotate the peer order by CTA and chunk so the SMs spread their
+                            // traffic over all destinations instead of all hitting one peer.
+                            const int g0 = static_cast<int>(blockIdx.x + c + q) % p.npeers;
+                            for (int i = 0; i < p.npeers; ++i) {
+                                const int g = g0 + i < p.npeers ? g0 + i : g0 + i - p.npeers;
+                                tma_store_2d(&peers.map[g], sbuf, col, row0);
+                            }
                         }
                         bulk_commit_group();
                     }
@@ -471,8 +477,11 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                             if (row0 + r >= p.m || pcol >= p.n) continue;
                             const uint4 v = ld_shared_v4(sbuf + r * 128 + ((piece ^ (r & 7)) << 4));
                             const long long off = (static_cast<long long>(row0 + r) * p.ldd + pcol) * kElem;
-                            for (int g = 0; g < p.npeers; ++g)
+                            const int g0 = static_cast<int>(blockIdx.x + c + q) % p.npeers;
+                            for (int i = 0; i < p.npeers; ++i) {
+                                const int g = g0 + i < p.npeers ? g0 + i : g0 + i - p.npeers;
                                 *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_d[g]) + off) = v;
+                            }
                         }
                     }
                     buf ^= 1;
