@@ -5,7 +5,7 @@
 # as the "cublaslt_p35" candidate for the reference's five frozen shapes.
 # Usage: sh baseline/build_ref_bridge.sh [/path/to/reference]
 set -e
-REF="${1:-/root/reference}"
+REF="${1:?usage: sh baseline/build_ref_bridge.sh /path/to/reference}"
 HERE="$(cd "$(dirname "$0")" && pwd)"
 mkdir -p "$HERE/_ref"
 nvcc -O3 -std=c++17 -shared -Xcompiler -fPIC \

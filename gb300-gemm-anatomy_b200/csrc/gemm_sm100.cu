@@ -7,25 +7,30 @@
 // candidate table gemm_comparison.py:214-265). Layout contract "TN":
 // A M x K row-major, B N x K row-major, D M x N row-major (gemm_comparison.py:2670-2691).
 //
-// One CTA per SM (1-CTA mode) or one CTA pair per two SMs (2-CTA mode,
-// tcgen05 cta_group::2), 192 threads:
-//   warp 0      TMA producer: one elected lane streams 128x64 A and Bx64 B
-//               K-slices into a ring of `kStages` 128B-swizzled SMEM slots,
-//               guarded by full/empty mbarriers.
-//   warp 1      allocates 512 TMEM columns; one elected lane (leader CTA
-//               only in 2-CTA mode) issues tcgen05.mma kind::f16 into a
-//               double-buffered 128x256 fp32 accumulator and frees ring slots
-//               with tcgen05.commit.
+// One CTA per SM (1-CTA mode) or one CTA pair per two SMs (tcgen05
+// cta_group::2), 192 threads:
+//   warp 0      TMA producer: one elected lane streams 128*sub_m x 64 A and
+//               (256/cta_group) x 64 B K-slices into a ring of `kStages`
+//               128B-swizzled SMEM slots, guarded by full/empty mbarriers. The
+//               leader's producer also takes tile ids from a global counter and
+//               publishes them through a shared-memory queue (dynamic schedule).
+//   warp 1      allocates all 512 TMEM columns; one elected lane (leader CTA
+//               only in pair mode) issues tcgen05.mma kind::f16 into 128 x 256
+//               fp32 accumulators ("units") rotating through two TMEM slots,
+//               and frees ring slots with tcgen05.commit.
 //   warps 2..5  epilogue: tcgen05.ld 32 rows each -> bf16/fp32 -> swizzled
-//               SMEM staging -> TMA store; the accumulator buffer is handed
-//               back to the MMA warp as soon as its last columns are in
-//               registers, so the epilogue of tile i overlaps the MMAs of i+1.
-// Tiles are walked persistently in an M-grouped raster for L2 reuse.
+//               SMEM staging -> TMA store (and, for the fused multi-GPU gather,
+//               the same chunk to every peer's D); a unit's TMEM slot is handed
+//               back as soon as it is in registers, so the epilogue overlaps the
+//               next MMAs.
+// Tile shapes: 128 x 256 (1-CTA), 256 x 256 per pair (sub_m = 1, successive
+// tiles double-buffer TMEM) and 512 x 256 per pair (sub_m = 2, a tile's two
+// row halves fill TMEM; 25 % fewer L2->SM bytes per FLOP).
 //
-// 2-CTA mode: the pair computes a 256x256 tile with M=256 MMAs issued by the
-// even CTA. Each CTA loads its own 128 A rows and 128 B rows (unicast TMA)
-// and signals the leader's full barrier; the leader's commits are sent to each
-// CTA's barrier separately (two unicast commits, no multicast anywhere).
+// Pair mode: M = 256 MMAs issued by the even CTA. Each CTA loads its own A
+// rows and its half of B (unicast TMA) and signals the leader's full barrier;
+// the leader's commits are sent to each CTA's barrier separately (two unicast
+// commits, no multicast anywhere).
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
