@@ -48,6 +48,7 @@ DEV_STATUS_NAMES = {
     0x105: "TIMEOUT_STREAM",
     0x106: "TIMEOUT_UMMA",
     0x107: "TIMEOUT_SELFTEST",
+    0x108: "TIMEOUT_PARTIAL",
     0x1FF: "BAD_LAUNCH",
 }
 
@@ -124,6 +125,7 @@ SIGNATURES = {
     "b200_gemm_supported": (_INT, [_I64, _I64, _I64, _I64, _INT, _INT]),
     "b200_gemm": (_INT, [_I64, _I64, _I64, _P, _P, _P, _I64, _INT, _INT, _P]),
     "b200_gemm_plan_launches": (_I64, [_P]),
+    "b200_gemm_plan_schedule": (_INT, [_P]),
     "b200_gemm_plan_set_trace": (_INT, [_P, _P, _I64]),
     "b200_gemm_plan_set_peers": (_INT, [_P, _INT, ctypes.POINTER(_P)]),
     "b200_ipc_handle_size": (ctypes.c_size_t, []),

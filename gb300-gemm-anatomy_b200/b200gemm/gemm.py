@@ -81,6 +81,11 @@ class GemmPlan:
     def launches_per_execute(self) -> int:
         return int(self._lib.b200_gemm_plan_launches(self._plan))
 
+    @property
+    def schedule(self) -> str:
+        """'dynamic' (whole tiles from a global counter) or 'stream_k'."""
+        return "stream_k" if self._lib.b200_gemm_plan_schedule(self._plan) == 1 else "dynamic"
+
     def set_peers(self, peer_ptrs) -> None:
         """Fused gather: also write every output chunk into these peer buffers."""
         arr = (ctypes.c_void_p * max(len(peer_ptrs), 1))(*[ctypes.c_void_p(int(q)) for q in peer_ptrs])

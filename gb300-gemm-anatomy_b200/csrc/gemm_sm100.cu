@@ -101,6 +101,30 @@ struct GemmParams {
     int peer_tma;    // 1: peer chunks go out as TMA bulk stores (PeerMaps), 0: 16-byte stores
     long long ldd;
     void* peer_d[kMaxPeers];
+    // Stream-K schedule (sk_iters > 0; otherwise the dynamic schedule above).
+    // The clusters form sk_groups groups of sk_lanes; group g, lane l is
+    // cluster g * sk_lanes + l (clusters past the last group get no work). A
+    // group works on "super-tiles": with one lane a super-tile is a tile of
+    // the raster walk; with several it is one m-block (sk_lane_n = 1, lane l
+    // takes n-block l) or one n-block (lane l takes m-block l), so the tiles
+    // that share an A (or B) panel run the same k-slices at the same time.
+    // The first sk_iters / num_k_blocks super-tiles (the "split block") are
+    // cut into sk_groups equal runs of k-slices, one per group, run first;
+    // then `sk_rounds` rounds of whole super-tiles follow (split + j *
+    // sk_groups + g in round j), so every group ends at the same time on whole
+    // tiles and the reductions of the cut tiles overlap the later MMAs. A cut
+    // super-tile is finished by the group that runs its first k-slices (that
+    // group's last run) after every later group holding a run of it (their
+    // first run) has left its fp32 partial in its own slot of sk_partial and
+    // set its sk_flags word; the finisher adds the partials in k order, writes
+    // D and clears the flags.
+    int sk_rounds;
+    int sk_groups;
+    int sk_lanes;
+    int sk_lane_n;
+    long long sk_iters;   // k-slices in the split block (per lane)
+    float* sk_partial;    // [cluster][cta rank][sub_m][warp] x 32 x 256 fp32
+    int* sk_flags;        // same indexing, one int each; zero between launches
 };
 
 // Tensor maps of the peers' D slices for the TMA form of the fused gather.
@@ -118,6 +142,54 @@ __device__ __forceinline__ void trace_stamp(const GemmParams& p, int slot) {
         p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = globaltimer_ns();
 }
 
+// One unit of a cluster's work: super-tile t over k-slices [kb0, kb1).
+// role 0: the whole K range; 1: a run that does not start at k-slice 0 (its
+// partial goes to this cluster's slot); 2: a run from k-slice 0 that stops
+// short of K (finished with the partials of the later groups).
+struct WorkItem {
+    int t, kb0, kb1, role;
+};
+
+struct SkCursor {
+    int group, lane, round;
+    long long pos, end;
+};
+
+__device__ __forceinline__ long long sk_group_start(const GemmParams& p, int g) {
+    return static_cast<long long>(g) * p.sk_iters / p.sk_groups;
+}
+
+__device__ __forceinline__ void sk_begin(const GemmParams& p, int cluster, SkCursor& cur) {
+    cur.group = cluster / p.sk_lanes;
+    cur.lane = cluster - cur.group * p.sk_lanes;
+    cur.round = 0;
+    if (cur.group >= p.sk_groups) {  // spare cluster: no work
+        cur.round = p.sk_rounds;
+        cur.pos = cur.end = 0;
+        return;
+    }
+    cur.pos = sk_group_start(p, cur.group);
+    cur.end = sk_group_start(p, cur.group + 1);
+}
+
+// Next item of the cluster's static stream-K walk; false at the end. Every
+// role of a CTA walks the same sequence.
+__device__ __forceinline__ bool sk_next(const GemmParams& p, SkCursor& cur, WorkItem& w) {
+    const int nk = p.num_k_blocks;
+    if (cur.pos < cur.end) {
+        const long long tl = cur.pos / nk;
+        const int kb0 = static_cast<int>(cur.pos - tl * nk);
+        const int kb1 = static_cast<int>(min(static_cast<long long>(nk), kb0 + (cur.end - cur.pos)));
+        w = {static_cast<int>(tl), kb0, kb1, kb0 > 0 ? 1 : (kb1 < nk ? 2 : 0)};
+        cur.pos += kb1 - kb0;
+        return true;
+    }
+    if (cur.round >= p.sk_rounds) return false;
+    w = {static_cast<int>(p.sk_iters / nk) + cur.round * p.sk_groups + cur.group, 0, nk, 0};
+    ++cur.round;
+    return true;
+}
+
 // Linear tile id -> (m block, n block): M-grouped raster so that the tiles in
 // flight at one time share A rows and B rows in L2.
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mb, int& nb) {
@@ -132,6 +204,19 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mb,
     const int b = r / gsize;
     mb = p.raster_n ? b : a;
     nb = p.raster_n ? a : b;
+}
+
+// (m block, n block) of lane `lane`'s tile in super-tile t (stream-K).
+__device__ __forceinline__ void sk_tile_coords(int t, int lane, const GemmParams& p, int& mb, int& nb) {
+    if (p.sk_lanes == 1) {
+        tile_coords(t, p, mb, nb);
+    } else if (p.sk_lane_n) {
+        mb = t;
+        nb = lane;
+    } else {
+        mb = lane;
+        nb = t;
+    }
 }
 
 template <int kCtaGroup, int kSubM, bool kOutF32>
@@ -171,6 +256,9 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
     const int lane = threadIdx.x & 31;
     const uint32_t rank = kPair ? cluster_ctarank() : 0;
     const int num_clusters = gridDim.x / kCtaGroup;
+    const int cluster = blockIdx.x / kCtaGroup;
+    // Stream-K runs only with one accumulator per tile (see the epilogue's finisher).
+    const bool sk = kSubM == 1 && p.sk_iters > 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -229,10 +317,16 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
             bool ok = true;
             // The leader fetches the first tile id now and each later one while the
             // current tile is still loading (see fetch_kb).
-            int next = (rank == 0) ? atomicAdd(&p.tile_counter[0], 1) : -1;
+            int next = (rank == 0 && !sk) ? atomicAdd(&p.tile_counter[0], 1) : -1;
+            SkCursor cur;
+            if (sk) sk_begin(p, cluster, cur);
             while (ok) {
-                int t;
-                if (rank == 0) {
+                int t, kb0 = 0, kb1 = p.num_k_blocks;
+                if (sk) {
+                    WorkItem w;
+                    t = sk_next(p, cur, w) ? w.t : -1;
+                    if (t >= 0) { kb0 = w.kb0; kb1 = w.kb1; }
+                } else if (rank == 0) {
                     // Publish the prefetched tile id.
                     if (!mbar_wait(qempty0 + 8 * qs, qph ^ 1, p.status, p.timeout_ns,
                                    B200_DEV_TIMEOUT_PRODUCER)) {
@@ -266,7 +360,8 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     break;
                 }
                 int mb, nb;
-                tile_coords(t, p, mb, nb);
+                if (sk) sk_tile_coords(t, cur.lane, p, mb, nb);
+                else tile_coords(t, p, mb, nb);
                 const int a_row = mb * C::kTileM + static_cast<int>(rank) * C::kARows;
                 const int b_row = nb * kBN + static_cast<int>(rank) * C::kBRows;
                 // The next tile id is fetched late in this tile (two ring depths
@@ -274,8 +369,8 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 // trip, late enough that a fast pair cannot take two tiles while a
                 // slow one has none.
                 const int fetch_kb = max(0, p.num_k_blocks - 2 * kStages);
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-                    if (rank == 0 && kb == fetch_kb) next = atomicAdd(&p.tile_counter[0], 1);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!sk && rank == 0 && kb == fetch_kb) next = atomicAdd(&p.tile_counter[0], 1);
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.status, p.timeout_ns,
                                    B200_DEV_TIMEOUT_PRODUCER)) {
                         ok = false;
@@ -320,19 +415,29 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
             // barriers' phase flips every second unit.
             uint32_t stage = 0, phase = 0, unit = 0, qs = 0, qph = 0;
             bool ok = true;
+            SkCursor cur;
+            if (sk) sk_begin(p, cluster, cur);
             while (ok) {
-                if (!queue_wait(qs, qph, B200_DEV_TIMEOUT_MMA_FULL)) break;
-                const int t = ring[qs];
-                queue_release(qs);
-                if (++qs == kQueue) { qs = 0; qph ^= 1; }
-                if (t < 0) break;
+                int kb0 = 0, kb1 = p.num_k_blocks;
+                if (sk) {
+                    WorkItem w;
+                    if (!sk_next(p, cur, w)) break;
+                    kb0 = w.kb0;
+                    kb1 = w.kb1;
+                } else {
+                    if (!queue_wait(qs, qph, B200_DEV_TIMEOUT_MMA_FULL)) break;
+                    const int t = ring[qs];
+                    queue_release(qs);
+                    if (++qs == kQueue) { qs = 0; qph ^= 1; }
+                    if (t < 0) break;
+                }
                 // MMAs of row half `sm` for k-slice `kb` held in ring slot `st`; the
-                // first k-slice of a half waits for its TMEM slot, the last one
-                // signals the epilogue.
+                // item's first k-slice of a half waits for its TMEM slot (and
+                // overwrites the accumulator), the last one signals the epilogue.
                 auto issue_sub = [&](int sm, uint32_t st, int kb) -> bool {
                     const uint32_t u = unit + sm;
                     const uint32_t slot = u & 1;
-                    if (kb == 0) {
+                    if (kb == kb0) {
                         if (!mbar_wait<kPair>(tempty0 + 8 * slot, ((u >> 1) & 1) ^ 1, p.status,
                                               p.timeout_ns, B200_DEV_TIMEOUT_MMA_TMEM)) {
                             return false;
@@ -347,9 +452,9 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     for (int k = 0; k < kBK / 16; ++k) {
                         umma_bf16<kCtaGroup>(d_tmem, smem_desc_sw128(a_sub + 32 * k),
                                              smem_desc_sw128(sb + 32 * k), idesc,
-                                             (kb | k) != 0 ? 1u : 0u);
+                                             (kb != kb0 || k != 0) ? 1u : 0u);
                     }
-                    if (kb == p.num_k_blocks - 1) {
+                    if (kb == kb1 - 1) {
                         const uint32_t tb = tfull0 + 8 * slot;
                         if constexpr (!kPair) {
                             umma_commit<1>(tb);
@@ -381,21 +486,21 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 // `head` k-slices while the epilogue is still draining the second
                 // half's slot; those ring slots are held until the second half has
                 // used them too.
-                const int head = kSubM == 2 ? min(kStages, p.num_k_blocks) : 0;
+                const int head = kSubM == 2 ? min(kStages, kb1 - kb0) : 0;
                 if (head > 0) {
                     uint32_t st = stage, ph = phase;
-                    for (int kb = 0; ok && kb < head; ++kb) {
+                    for (int kb = kb0; ok && kb < kb0 + head; ++kb) {
                         ok = wait_full(st, ph) && issue_sub(0, st, kb);
                         if (++st == kStages) { st = 0; ph ^= 1; }
                     }
-                    for (int kb = 0; ok && kb < head; ++kb) {
+                    for (int kb = kb0; ok && kb < kb0 + head; ++kb) {
                         ok = issue_sub(1, stage, kb);
                         if (!ok) break;
                         release_stage(stage);
                         if (++stage == kStages) { stage = 0; phase ^= 1; }
                     }
                 }
-                for (int kb = head; ok && kb < p.num_k_blocks; ++kb) {
+                for (int kb = kb0 + head; ok && kb < kb1; ++kb) {
                     ok = wait_full(stage, phase);
 #pragma unroll
                     for (int sm = 0; ok && sm < kSubM; ++sm) ok = issue_sub(sm, stage, kb);
@@ -415,18 +520,122 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         uint32_t unit = 0, buf = 0, qs = 0, qph = 0;
         int local_tile = 0;
         bool ok = true;
+        SkCursor cur;
+        if (sk) sk_begin(p, cluster, cur);
         for (; ok; ++local_tile) {
-            if (!queue_wait(qs, qph, B200_DEV_TIMEOUT_EPILOGUE)) break;
-            const int t = ring[qs];
-            __syncwarp();
-            if (lane == 0) queue_release(qs);
-            if (++qs == kQueue) { qs = 0; qph ^= 1; }
+            int t, role = 0;
+            if (sk) {
+                WorkItem w;
+                t = sk_next(p, cur, w) ? w.t : -1;
+                if (t >= 0) role = w.role;
+            } else {
+                if (!queue_wait(qs, qph, B200_DEV_TIMEOUT_EPILOGUE)) break;
+                t = ring[qs];
+                __syncwarp();
+                if (lane == 0) queue_release(qs);
+                if (++qs == kQueue) { qs = 0; qph ^= 1; }
+            }
             if (t < 0) break;
             int mb, nb;
-            tile_coords(t, p, mb, nb);
+            if (sk) sk_tile_coords(t, cur.lane, p, mb, nb);
+            else tile_coords(t, p, mb, nb);
             const int col0 = nb * kBN;
+            // A finisher (role 2) adds the partials of the later groups whose runs
+            // lie inside this super-tile, in k order: groups group+1 .. group+nwriters.
+            int nwriters = 0;
+            if (role == 2) {
+                const long long tile_end = static_cast<long long>(t + 1) * p.num_k_blocks;
+                while (cur.group + 1 + nwriters < p.sk_groups &&
+                       sk_group_start(p, cur.group + 1 + nwriters) < tile_end) {
+                    ++nwriters;
+                }
+            }
             for (int sm = 0; sm < kSubM; ++sm, ++unit) {
                 const uint32_t slot = unit & 1;
+                const int row0 = mb * C::kTileM + static_cast<int>(rank) * C::kARows +
+                                 sm * kRowsPerCta + q * 32;
+                const uint32_t t_row = tmem_base + slot * kBN + (static_cast<uint32_t>(q * 32) << 16);
+                // Stream-K partial of this warp's 32 x 256 accumulator block, kept in
+                // the slot of the cluster that computed it, laid out [32-column
+                // chunk][float4 column group][lane] so that every warp access is 512
+                // contiguous bytes.
+                auto slot_of = [&](int cl) -> long long {
+                    return ((static_cast<long long>(cl) * kCtaGroup + rank) * kSubM + sm) * kEpiWarps + q;
+                };
+                auto writer_cluster = [&](int w) { return (cur.group + 1 + w) * p.sk_lanes + cur.lane; };
+                auto partial_src = [&](int w) {
+                    return reinterpret_cast<const float4*>(p.sk_partial) +
+                           slot_of(writer_cluster(w)) * (32 * kBN / 4) + lane;
+                };
+                // Without whole-tile rounds after the split block a finisher's item is
+                // the CTA's last, so the other TMEM slot is free: the partials are
+                // summed into it while the item's MMAs still run, and only TMEM reads
+                // remain at the end. With rounds to follow, the partials are added
+                // from L2 while the next whole tile's MMAs run.
+                const bool stage_in_tmem = p.sk_rounds == 0;
+                const uint32_t t_stage = tmem_base + (slot ^ 1) * kBN + (static_cast<uint32_t>(q * 32) << 16);
+                if (role == 2) {
+                    // Wait (bounded) for every later run's partial.
+                    bool got = true;
+#pragma unroll 1
+                    for (int w = 0; w < nwriters && got; ++w) {
+                        const int* flag = p.sk_flags + slot_of(writer_cluster(w));
+                        got = ld_acquire_gpu(flag) != 0;
+                        const uint64_t t0 = globaltimer_ns();
+                        while (!got) {
+#pragma unroll 1
+                            for (int i = 0; i < 32 && !got; ++i) got = ld_acquire_gpu(flag) != 0;
+                            if (got || status_failed(p.status)) break;
+                            if (globaltimer_ns() - t0 > p.timeout_ns) {
+                                report_status(p.status, B200_DEV_TIMEOUT_PARTIAL);
+                                break;
+                            }
+                        }
+                    }
+                    if (!__all_sync(0xffffffffu, got)) {
+                        ok = false;
+                        break;
+                    }
+                    // Consumed in this launch; the next launch's writers set them again.
+                    for (int w = lane; w < nwriters; w += 32) p.sk_flags[slot_of(writer_cluster(w))] = 0;
+                    if (stage_in_tmem) {
+                        // Four 32-column chunks (16 KB per warp) in flight per batch: the
+                        // loads are latency-bound, so their count in flight sets the speed.
+                        constexpr int kBatch = kCtaGroup == 2 ? 4 : 1;
+#pragma unroll 1
+                        for (int c0 = 0; c0 < kBN / 32; c0 += kBatch) {
+                            uint32_t r[kBatch][32];
+#pragma unroll
+                            for (int j = 0; j < kBatch; ++j) {
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) {
+                                    const float4 v = __ldcg(partial_src(0) + ((c0 + j) * 8 + i) * 32);
+                                    r[j][4 * i] = __float_as_uint(v.x);
+                                    r[j][4 * i + 1] = __float_as_uint(v.y);
+                                    r[j][4 * i + 2] = __float_as_uint(v.z);
+                                    r[j][4 * i + 3] = __float_as_uint(v.w);
+                                }
+                            }
+#pragma unroll 1
+                            for (int w = 1; w < nwriters; ++w) {
+#pragma unroll
+                                for (int j = 0; j < kBatch; ++j) {
+#pragma unroll
+                                    for (int i = 0; i < 8; ++i) {
+                                        const float4 v = __ldcg(partial_src(w) + ((c0 + j) * 8 + i) * 32);
+                                        r[j][4 * i] = __float_as_uint(__uint_as_float(r[j][4 * i]) + v.x);
+                                        r[j][4 * i + 1] = __float_as_uint(__uint_as_float(r[j][4 * i + 1]) + v.y);
+                                        r[j][4 * i + 2] = __float_as_uint(__uint_as_float(r[j][4 * i + 2]) + v.z);
+                                        r[j][4 * i + 3] = __float_as_uint(__uint_as_float(r[j][4 * i + 3]) + v.w);
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int j = 0; j < kBatch; ++j) tmem_st_32x32b_x32(t_stage + (c0 + j) * 32, r[j]);
+                        }
+                        tmem_st_wait();
+                    }
+                }
                 if (!mbar_wait<kPair, true>(tfull0 + 8 * slot, (unit >> 1) & 1, p.status,
                                             p.timeout_ns, B200_DEV_TIMEOUT_EPILOGUE)) {
                     ok = false;
@@ -434,9 +643,43 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 }
                 if (sm == 0 && warp == 2 && lane == 0) trace_stamp(p, 6 + local_tile);
                 tc_fence_after();
-                const int row0 = mb * C::kTileM + static_cast<int>(rank) * C::kARows +
-                                 sm * kRowsPerCta + q * 32;
-                const uint32_t t_row = tmem_base + slot * kBN + (static_cast<uint32_t>(q * 32) << 16);
+                // Finisher: accumulator + partials (summed in k order of the runs).
+                auto add_partial = [&](int c32, uint32_t (&r)[32]) {
+                    if (stage_in_tmem) {
+                        uint32_t t[32];
+                        tmem_ld_32x32b_x32(t_stage + c32 * 32, t);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(t[i]));
+                        return;
+                    }
+                    // Sum of the partials in k order first, then onto the accumulator:
+                    // the same association as the TMEM-staged path.
+                    float4 acc[8];
+#pragma unroll 1
+                    for (int w = 0; w < nwriters; ++w) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 v = __ldcg(partial_src(w) + (c32 * 8 + i) * 32);
+                            if (w == 0) {
+                                acc[i] = v;
+                            } else {
+                                acc[i].x += v.x;
+                                acc[i].y += v.y;
+                                acc[i].z += v.z;
+                                acc[i].w += v.w;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) + acc[i].x);
+                        r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) + acc[i].y);
+                        r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) + acc[i].z);
+                        r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) + acc[i].w);
+                    }
+                };
                 // Stage one 32-row x 128-byte chunk of this warp's rows and TMA-store it.
                 auto store_chunk = [&](int c, const uint32_t* packed) {
                     // Chunks wholly outside D are skipped before touching the staging
@@ -500,6 +743,30 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         else mbar_arrive_cluster(mapa_shared(tempty0 + 8 * slot, 0));
                     }
                 };
+                if (role == 1) {
+                    // A run that does not start at k-slice 0: leave the fp32 partial in
+                    // this cluster's slot for the finisher; D is not written.
+                    float4* part = reinterpret_cast<float4*>(p.sk_partial) +
+                                   slot_of(cluster) * (32 * kBN / 4) + lane;
+                    int* flag = p.sk_flags + slot_of(cluster);
+#pragma unroll 1
+                    for (int c = 0; c < kBN / 32; ++c) {
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(t_row + c * 32, r);
+                        tmem_ld_wait();
+                        if (c == kBN / 32 - 1) release_tmem();
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            __stcg(part + (c * 8 + i) * 32,
+                                   make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                               __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])));
+                        }
+                    }
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) st_release_gpu(flag, 1);
+                    continue;
+                }
                 if constexpr (kOutF32) {
 #pragma unroll 1
                     for (int c = 0; c < kChunks; ++c) {
@@ -507,7 +774,27 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         tmem_ld_32x32b_x32(t_row + c * 32, packed);
                         tmem_ld_wait();
                         if (c == kChunks - 1) release_tmem();
+                        if (role == 2) add_partial(c, packed);
                         store_chunk(c, packed);
+                    }
+                } else if (role == 2) {
+                    // bf16 finisher: one 64-column chunk at a time (the partial sums
+                    // need the registers the drain-all path below keeps packed rows in).
+#pragma unroll 1
+                    for (int c = 0; c < kChunks; ++c) {
+                        uint32_t r0[32], r1[32], pk[32];
+                        tmem_ld_32x32b_x32(t_row + c * 64, r0);
+                        tmem_ld_32x32b_x32(t_row + c * 64 + 32, r1);
+                        tmem_ld_wait();
+                        if (c == kChunks - 1) release_tmem();
+                        add_partial(2 * c, r0);
+                        add_partial(2 * c + 1, r1);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            pk[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+                            pk[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+                        }
+                        store_chunk(c, pk);
                     }
                 } else {
                     // bf16: the whole 256-column row fits in 128 registers once
@@ -590,6 +877,7 @@ struct B200Plan {
     int grid = 0;
     int smem = 0;
     int* d_status = nullptr;
+    size_t words_bytes = 0;  // device words reset after a failed launch (status, counter, stream-K flags)
     bool empty_problem = false;
     B200PlanInfo info{};
 };
@@ -597,6 +885,69 @@ struct B200Plan {
 namespace b200 {
 
 constexpr size_t kPlanWordsBytes = 16;  // status word, pad, 2-int tile counter
+
+// Stream-K layout for a plan with `slots` resident clusters; returns false
+// (p untouched) for the dynamic schedule. Lanes: when one side of the tile
+// grid is at most 4 blocks wide, each group holds one lane per block of that
+// side, so the tiles sharing an A (or B) panel stream the same k-slices at the
+// same time and the panel crosses HBM once. A super-tile is cut into at most
+// four runs (each group's run is at least a third of K). Only tiles with one
+// accumulator per CTA (1-CTA 128 x 256, pair 256 x 256) qualify: the finisher
+// adds the partials while later MMAs run. Auto: used when the dynamic
+// schedule's last wave would leave more than 10 % of the clusters idle on
+// average (busy = waves / ceil(waves) < 0.9) and it runs at least three waves:
+// a cut tile costs its CTAs an extra 128 KB out and back through L2 in the
+// epilogue (measured on B200 with per-CTA timer stamps: 7-9 us for the run
+// that writes a partial, 11-17 us for the finisher, against ~4 us for a whole
+// tile with fp32 D), which whole-tile rounds after the split block absorb.
+// Measured: 4096^3 and 32768 x 512 x 4096 (3.46 waves) gain 1-3 %; the
+// 1.73-wave shapes 16384 x 512 x 4096 and 512 x 16384 x 4096 lose ~3 %.
+// B200_GEMM_SCHEDULE=dynamic or =streamk overrides the choice (still subject
+// to the tile-shape and run-length rules).
+static bool stream_k_layout(GemmParams& p, int slots, int sub_m) {
+    if (sub_m != 1) return false;
+    bool forced = false;
+    if (const char* e = std::getenv("B200_GEMM_SCHEDULE")) {
+        if (e[0] == 'd') return false;
+        forced = e[0] == 's';
+    }
+    if (slots < 2 || p.num_tiles < 2) return false;
+    if (!forced) {
+        const double w = static_cast<double>(p.num_tiles) / slots;
+        if (w < 3.0 || w / std::ceil(w) >= 0.9) return false;
+    }
+    int lanes = 1, lane_n = 0;
+    if (p.num_n_blocks <= 4 && p.num_n_blocks <= p.num_m_blocks) {
+        lanes = p.num_n_blocks;
+        lane_n = 1;
+    } else if (p.num_m_blocks <= 4) {
+        lanes = p.num_m_blocks;
+    }
+    const int groups = slots / lanes;
+    const long long supers = lanes == 1 ? p.num_tiles : (lane_n ? p.num_m_blocks : p.num_n_blocks);
+    if (groups < 2) return false;
+    // Split block: the super-tiles left over after whole rounds, or one round
+    // more when they are too few for runs of a third of K.
+    const long long rounds = supers / groups;
+    const long long rest = supers - rounds * groups;
+    long long split;
+    if (rest == 0) return false;  // whole rounds fill every group already
+    if (rest * 3 >= groups) split = rest;
+    else if (rounds >= 1) split = rest + groups;
+    else return false;
+    p.sk_lanes = lanes;
+    p.sk_lane_n = lane_n;
+    p.sk_groups = groups;
+    p.sk_rounds = static_cast<int>((supers - split) / groups);
+    p.sk_iters = split * p.num_k_blocks;
+    return true;
+}
+
+// Bytes of the stream-K partial buffer: one 32 x 256 fp32 block per
+// (cluster slot, CTA of the pair, row half, epilogue warp).
+static size_t stream_k_partial_bytes(int clusters, int cta_group, int sub_m) {
+    return static_cast<size_t>(clusters) * cta_group * sub_m * kEpiWarps * 32 * kBN * sizeof(float);
+}
 
 static int check_shape(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dtype, int mode) {
     if (out_dtype != B200_OUT_BF16 && out_dtype != B200_OUT_F32) {
@@ -750,21 +1101,7 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
     raster_for(p, tile_m, plan->sub_m, &p.group_m, &p.raster_n);
     p.timeout_ns = wait_timeout_ns();
 
-    // Device words of the plan: [0] status, [2..3] tile scheduler counter.
-    cudaError_t err = cudaMalloc(&plan->d_status, kPlanWordsBytes);
-    if (err != cudaSuccess) {
-        delete plan;
-        return cuda_fail("cudaMalloc(status word)", err);
-    }
-    err = cudaMemset(plan->d_status, 0, kPlanWordsBytes);
-    if (err != cudaSuccess) {
-        cudaFree(plan->d_status);
-        delete plan;
-        return cuda_fail("cudaMemset(status word)", err);
-    }
-    p.status = plan->d_status;
-    p.tile_counter = plan->d_status + 2;
-
+    cudaError_t err = cudaSuccess;
     int slots = 0;
     if (!empty) {
         rc = encode_tmap_2d(&plan->tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, m, k, k,
@@ -781,7 +1118,6 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
                                     64, CU_TENSOR_MAP_SWIZZLE_128B);
         }
         if (rc != B200_OK) {
-            cudaFree(plan->d_status);
             delete plan;
             return rc;
         }
@@ -791,7 +1127,6 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
         if (err == cudaSuccess && plan->cta_group == 2)
             err = cudaFuncSetAttribute(sym, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
         if (err != cudaSuccess) {
-            cudaFree(plan->d_status);
             delete plan;
             return cuda_fail("cudaFuncSetAttribute", err);
         }
@@ -819,6 +1154,38 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
         }
         const int clusters = std::min(p.num_tiles, slots);
         plan->grid = clusters * plan->cta_group;
+        if (stream_k_layout(p, slots, plan->sub_m)) plan->grid = p.sk_groups * p.sk_lanes * plan->cta_group;
+    }
+
+    // Device words of the plan: [0] status, [2..3] tile scheduler counter; with
+    // stream-K also the flags (from byte 256) and the partial buffer (after them).
+    const int sk_clusters = plan->grid / plan->cta_group;
+    const size_t flags_off = 256;
+    const size_t flags_bytes =
+        p.sk_iters > 0 ? static_cast<size_t>(sk_clusters) * plan->cta_group * plan->sub_m * kEpiWarps * sizeof(int)
+                       : 0;
+    const size_t part_off = (flags_off + flags_bytes + 255) / 256 * 256;
+    plan->words_bytes = p.sk_iters > 0 ? flags_off + flags_bytes : kPlanWordsBytes;
+    const size_t alloc_bytes =
+        p.sk_iters > 0 ? part_off + stream_k_partial_bytes(sk_clusters, plan->cta_group, plan->sub_m)
+                       : kPlanWordsBytes;
+    err = cudaMalloc(&plan->d_status, alloc_bytes);
+    if (err != cudaSuccess) {
+        delete plan;
+        return cuda_fail("cudaMalloc(plan device words)", err);
+    }
+    err = cudaMemset(plan->d_status, 0, plan->words_bytes);
+    if (err != cudaSuccess) {
+        cudaFree(plan->d_status);
+        delete plan;
+        return cuda_fail("cudaMemset(plan device words)", err);
+    }
+    p.status = plan->d_status;
+    p.tile_counter = plan->d_status + 2;
+    if (p.sk_iters > 0) {
+        uint8_t* base = reinterpret_cast<uint8_t*>(plan->d_status);
+        p.sk_flags = reinterpret_cast<int*>(base + flags_off);
+        p.sk_partial = reinterpret_cast<float*>(base + part_off);
     }
 
     B200PlanInfo& info = plan->info;
@@ -953,7 +1320,7 @@ int b200_stream_synchronize(B200Plan* plan) {
     B200_CUDA_TRY(cudaMemcpy(&status, plan->d_status, sizeof(int), cudaMemcpyDeviceToHost));
     if (status != 0) {
         // An aborted launch may leave the tile counter mid-walk: re-arm it too.
-        B200_CUDA_TRY(cudaMemset(plan->d_status, 0, b200::kPlanWordsBytes));
+        B200_CUDA_TRY(cudaMemset(plan->d_status, 0, plan->words_bytes));
         b200::set_error("GEMM kernel reported device status 0x%x (%s)", status,
                         status == B200_DEV_BAD_LAUNCH ? "launch contract violated"
                                                       : "bounded wait timed out");
@@ -1020,6 +1387,11 @@ int b200_gemm_plan_set_trace(B200Plan* plan, unsigned long long* trace, int64_t 
     }
     plan->params.trace = trace;
     return B200_OK;
+}
+
+int b200_gemm_plan_schedule(const B200Plan* plan) {
+    if (plan == nullptr) return -1;
+    return plan->params.sk_iters > 0 ? B200_SCHEDULE_STREAM_K : B200_SCHEDULE_DYNAMIC;
 }
 
 int64_t b200_gemm_plan_launches(const B200Plan* plan) {

@@ -51,6 +51,7 @@ enum {
     B200_DEV_TIMEOUT_STREAM = 0x105,   /* memory-path streamer waited too long for a stage */
     B200_DEV_TIMEOUT_UMMA = 0x106,     /* UMMA probe waited too long for its commit */
     B200_DEV_TIMEOUT_SELFTEST = 0x107, /* b200_selftest_bounded_wait ran out, as designed */
+    B200_DEV_TIMEOUT_PARTIAL = 0x108,  /* stream-K epilogue waited too long for a partial tile */
     B200_DEV_BAD_LAUNCH = 0x1FF        /* launch geometry differs from the kernel's contract */
 };
 
@@ -221,6 +222,18 @@ int b200_gemm_plan_set_trace(B200Plan* plan, unsigned long long* trace, int64_t 
 
 /* Number of device kernels one execute launches (for launch accounting). */
 int64_t b200_gemm_plan_launches(const B200Plan* plan);
+
+/* Tile schedule a plan runs. DYNAMIC: whole tiles handed out by a global
+ * counter. STREAM_K: when the last wave of whole tiles would leave clusters
+ * idle, the last tiles are split along K into equal runs per cluster, the
+ * cut tiles finished through an fp32 partial buffer the plan allocates
+ * (this ties each result's summation split to the device's SM count). The
+ * environment variable B200_GEMM_SCHEDULE=dynamic|streamk overrides the
+ * choice at plan creation. No counterpart in the reference, whose persistent
+ * CuTe kernel (src/gemm/gemm_comparison.py candidate table) runs whole tiles.
+ * Returns -1 for a NULL plan. */
+enum { B200_SCHEDULE_DYNAMIC = 0, B200_SCHEDULE_STREAM_K = 1 };
+int b200_gemm_plan_schedule(const B200Plan* plan);
 
 /* ------------------------------------------------------------------------ */
 /* Memory path: global -> shared streaming (LDGSTS / TMA)                     */

@@ -1,0 +1,143 @@
+"""Stream-K schedule: tiles of the last wave split along K between clusters.
+
+Parity of the split path through the C ABI, for both kernel shapes that run it
+(1-CTA 128x256, pair 256x256) and both output types:
+  integer operands (the reference's factory): fp32 D exact (max_abs_error 0);
+  seeded uniform operands: the bf16 rule of the other GEMM tests against a
+  float64 product, and fp32 D within 2^-20 * K of it (accumulation order only);
+  repeated launches of one plan give identical bits (the partial flags are
+  consumed and cleared inside every launch).
+"""
+import pytest
+import torch
+
+from b200gemm import check, gemm as G, operands
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def maxabs(t):
+    return float(t.float().abs().max()) if t.numel() else 0.0
+
+
+def plan_run(a_d, b_d, out_dtype, mode, repeats=1):
+    out = torch.full((a_d.shape[0], b_d.shape[0]), float("nan"), dtype=out_dtype, device=DEV)
+    plan = G.GemmPlan(a_d, b_d, out, mode=mode)
+    try:
+        sched = plan.schedule
+        plan.execute()
+        plan.synchronize()
+        first = out.clone()
+        for _ in range(repeats - 1):
+            out.fill_(float("nan"))
+            plan.execute()
+        plan.synchronize()
+        assert torch.equal(first, out), "repeated launches differ"
+    finally:
+        plan.destroy()
+    return out, sched
+
+
+# Shapes with an uneven last wave on a 148-SM B200 (1-CTA: 148 clusters of
+# 128x256 tiles; pairs: 74 clusters), ragged edges, K that is not a whole
+# number of 64-wide k-slices, and skinny grids (one side <= 4 blocks) where the
+# clusters run in lanes and a tile is cut into up to four runs.
+CASES = [
+    ("1cta", (2560, 2048, 328)),       # 160 tiles over 148 CTAs
+    ("1cta", (2500, 2000, 1024)),      # ragged M and N
+    ("1cta", (8192, 512, 2048)),       # lanes along N (2), 64 m-blocks
+    ("2cta", (2304, 2304, 520)),       # 81 tiles over 74 pairs
+    ("2cta", (4096, 512, 1024)),       # lanes along N: 16 super-tiles over 37 groups
+    ("2cta", (512, 8192, 4096)),       # lanes along M: 32 super-tiles over 37 groups
+    ("2cta", (4000, 1304, 4096)),      # 96 tiles, ragged, long K
+    ("2cta", (1000, 3000, 3000)),      # 4 m-blocks as lanes, ragged everything
+    ("2cta", (5000, 2104, 200)),       # 180 tiles, ragged, 4 k-slices
+    ("2cta", (16384, 512, 4096)),      # the reference's skinny frozen shape
+    ("2cta", (512, 16384, 4096)),      # and its transpose
+]
+
+
+@pytest.mark.parametrize("mode,shape", CASES)
+def test_stream_k_uniform(monkeypatch, mode, shape):
+    monkeypatch.setenv("B200_GEMM_SCHEDULE", "streamk")
+    m, n, k = shape
+    a, b = operands.uniform_operands(m, n, k, seed=11)
+    a_d, b_d = a.to(DEV), b.to(DEV)
+    ref = (a_d.double() @ b_d.double().T).cpu()
+    d, sched = plan_run(a_d, b_d, torch.bfloat16, mode, repeats=3)
+    assert sched == "stream_k", f"{mode} {shape}: schedule {sched}"
+    check.bf16_tolerance_check(f"{shape}/{mode}/sk", ref, d.cpu(), k, maxabs(a), maxabs(b))
+    d32, _ = plan_run(a_d, b_d, torch.float32, mode, repeats=3)
+    assert float((d32.cpu().double() - ref).abs().max()) <= 2.0 ** -20 * k
+
+
+@pytest.mark.parametrize("mode", ["1cta", "2cta"])
+def test_stream_k_integer_exact(monkeypatch, mode):
+    monkeypatch.setenv("B200_GEMM_SCHEDULE", "streamk")
+    m, n, k = {"1cta": (2560, 2048, 1024), "2cta": (2304, 2304, 1024)}[mode]
+    a, b = operands.integer_operands(m, n, k)
+    a_d, b_d = a.to(DEV), b.to(DEV)
+    d, sched = plan_run(a_d, b_d, torch.float32, mode, repeats=2)
+    assert sched == "stream_k"
+    ref = a_d.float() @ b_d.float().T  # integer products and sums: exact in fp32
+    assert torch.equal(d, ref)
+
+
+def test_two_accumulator_tiles_stay_dynamic(monkeypatch):
+    """512 x 256 pair tiles fill both TMEM slots: even when forced they keep the dynamic schedule."""
+    monkeypatch.setenv("B200_GEMM_SCHEDULE", "streamk")
+    m, n, k = 4608, 2304, 1024
+    a, b = operands.integer_operands(m, n, k)
+    a_d, b_d = a.to(DEV), b.to(DEV)
+    d, sched = plan_run(a_d, b_d, torch.float32, "2cta_m512")
+    assert sched == "dynamic"
+    assert torch.equal(d, a_d.float() @ b_d.float().T)
+
+
+def test_auto_picks_stream_k_on_an_uneven_last_wave(monkeypatch):
+    """4096^3 on 74 pairs: 256 tiles = 3.46 waves -> stream-K; 8192^2 x 512 -> dynamic."""
+    monkeypatch.delenv("B200_GEMM_SCHEDULE", raising=False)
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("schedule thresholds are stated for a 148-SM B200")
+    a, b = operands.uniform_operands(4096, 4096, 4096, seed=12)
+    a_d, b_d = a.to(DEV), b.to(DEV)
+    d_sk, sched = plan_run(a_d, b_d, torch.bfloat16, "auto")
+    assert sched == "stream_k"
+    monkeypatch.setenv("B200_GEMM_SCHEDULE", "dynamic")
+    d_dyn, sched = plan_run(a_d, b_d, torch.bfloat16, "auto")
+    assert sched == "dynamic"
+    ref = (a_d.double() @ b_d.double().T).cpu()
+    check.bf16_tolerance_check("4096^3/sk", ref, d_sk.cpu(), 4096, maxabs(a), maxabs(b))
+    check.bf16_tolerance_check("4096^3/dyn", ref, d_dyn.cpu(), 4096, maxabs(a), maxabs(b))
+    monkeypatch.delenv("B200_GEMM_SCHEDULE")
+    a2, b2 = operands.uniform_operands(8192, 8192, 512, seed=13)
+    out = torch.empty((8192, 8192), dtype=torch.bfloat16, device=DEV)
+    plan = G.GemmPlan(a2.to(DEV), b2.to(DEV), out)
+    try:
+        assert plan.schedule == "dynamic"  # 32 x 32 tiles of 256 x 256 / 74 = 13.8 waves
+    finally:
+        plan.destroy()
+
+
+def test_stream_k_back_to_back_launches(monkeypatch):
+    """Launches queued without a host sync (PDL overlaps their setup): same bits every time."""
+    monkeypatch.setenv("B200_GEMM_SCHEDULE", "streamk")
+    m, n, k = 2304, 2304, 2048
+    a, b = operands.uniform_operands(m, n, k, seed=14)
+    a_d, b_d = a.to(DEV), b.to(DEV)
+    outs = [torch.empty((m, n), dtype=torch.float32, device=DEV) for _ in range(2)]
+    plans = [G.GemmPlan(a_d, b_d, o, mode="2cta") for o in outs]
+    try:
+        assert all(p.schedule == "stream_k" for p in plans)
+        for i in range(20):
+            plans[i % 2].execute()
+        plans[0].synchronize()
+        plans[1].synchronize()
+    finally:
+        for p in plans:
+            p.destroy()
+    assert torch.equal(outs[0], outs[1])
+    ref = a_d.double() @ b_d.double().T
+    assert float((outs[0].double() - ref).abs().max()) <= 2.0 ** -20 * k
