@@ -125,6 +125,10 @@ struct GemmParams {
     long long sk_iters;   // k-slices in the split block (per lane)
     float* sk_partial;    // [cluster][cta rank][sub_m][warp] x 32 x 256 fp32
     int* sk_flags;        // same indexing, one int each; zero between launches
+    // Failure-path test hook (B200_TEST_DROP_PARTIAL_FLAGS at plan creation):
+    // partial writers skip their flag, so finishers' bounded waits run out and
+    // report B200_DEV_TIMEOUT_PARTIAL. Nothing faults or hangs.
+    int sk_test_drop_flags;
 };
 
 // Tensor maps of the peers' D slices for the TMA form of the fused gather.
@@ -764,7 +768,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     }
                     __threadfence();
                     __syncwarp();
-                    if (lane == 0) st_release_gpu(flag, 1);
+                    if (lane == 0 && !p.sk_test_drop_flags) st_release_gpu(flag, 1);
                     continue;
                 }
                 if constexpr (kOutF32) {
@@ -1154,7 +1158,10 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
         }
         const int clusters = std::min(p.num_tiles, slots);
         plan->grid = clusters * plan->cta_group;
-        if (stream_k_layout(p, slots, plan->sub_m)) plan->grid = p.sk_groups * p.sk_lanes * plan->cta_group;
+        if (stream_k_layout(p, slots, plan->sub_m)) {
+            plan->grid = p.sk_groups * p.sk_lanes * plan->cta_group;
+            if (const char* e = std::getenv("B200_TEST_DROP_PARTIAL_FLAGS")) p.sk_test_drop_flags = e[0] == '1';
+        }
     }
 
     // Device words of the plan: [0] status, [2..3] tile scheduler counter; with
