@@ -56,6 +56,28 @@ def _worker(rank, world, port, q):
                     check.bf16_tolerance_check(f"rank {rank} p2p={p2p} {mode}", ref, full.cpu(), k,
                                                1.0, 1.0)
                 sg.destroy()
+        # Stream-K per shard (forced): cut tiles are finished by the epilogue that
+        # also sends the output chunks to the peers.
+        os.environ.pop("B200_PEER_STORES", None)
+        os.environ["B200_GEMM_SCHEDULE"] = "streamk"
+        try:
+            m2, n2, k2 = 2304, 2304 * world, 1024
+            a2, b2 = operands.uniform_operands(m2, n2, k2, seed=13)
+            s0, s1 = bdist.shard_bounds(n2, world, rank)
+            a2d, b2d = a2.to(dev), b2.to(dev)
+            ref2 = (a2d.double() @ b2d.double().T).cpu()
+            for p2p in (False, True):
+                sg = bdist.ShardedGemm(a2d, b2d[s0:s1].contiguous(), n2, mode="2cta", p2p=p2p)
+                assert sg._plan.schedule == "stream_k", sg._plan.schedule
+                for _ in range(2):
+                    full = sg.run("full")
+                    sg.synchronize()
+                    torch.cuda.synchronize()
+                    check.bf16_tolerance_check(f"rank {rank} p2p={p2p} stream-K", ref2, full.cpu(),
+                                               k2, 1.0, 1.0)
+                sg.destroy()
+        finally:
+            os.environ.pop("B200_GEMM_SCHEDULE", None)
         q.put((rank, True, ""))
     except Exception as exc:
         q.put((rank, False, repr(exc)))
