@@ -223,7 +223,9 @@ __device__ __forceinline__ void sk_tile_coords(int t, int lane, const GemmParams
     }
 }
 
-template <int kCtaGroup, int kSubM, bool kOutF32>
+// kStreamK selects the stream-K schedule at compile time, so the dynamic
+// schedule's kernels carry none of its code (it measured 0.4-1 % on them).
+template <int kCtaGroup, int kSubM, bool kOutF32, bool kStreamK>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmD, const GemmParams p,
@@ -262,7 +264,8 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
     const int num_clusters = gridDim.x / kCtaGroup;
     const int cluster = blockIdx.x / kCtaGroup;
     // Stream-K runs only with one accumulator per tile (see the epilogue's finisher).
-    const bool sk = kSubM == 1 && p.sk_iters > 0;
+    static_assert(!kStreamK || kSubM == 1, "stream-K needs one accumulator per tile");
+    constexpr bool sk = kStreamK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -845,15 +848,16 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmParams, PeerMaps);
 
 // Kernel variants: (cta_group, sub_m) in {(1,1), (2,1), (2,2)} x {bf16, fp32} D.
-template <int G, int S>
+template <int G, int S, bool K>
 static const void* kernel_sym_t(bool f32) {
-    return f32 ? reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<G, S, true>)
-               : reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<G, S, false>);
+    return f32 ? reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<G, S, true, K>)
+               : reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<G, S, false, K>);
 }
 
-static const void* kernel_sym(int cta_group, int sub_m, bool f32) {
-    if (cta_group == 1) return kernel_sym_t<1, 1>(f32);
-    return sub_m == 2 ? kernel_sym_t<2, 2>(f32) : kernel_sym_t<2, 1>(f32);
+static const void* kernel_sym(int cta_group, int sub_m, bool f32, bool stream_k) {
+    if (cta_group == 1) return stream_k ? kernel_sym_t<1, 1, true>(f32) : kernel_sym_t<1, 1, false>(f32);
+    if (sub_m == 2) return kernel_sym_t<2, 2, false>(f32);
+    return stream_k ? kernel_sym_t<2, 1, true>(f32) : kernel_sym_t<2, 1, false>(f32);
 }
 
 static int smem_bytes_for(int cta_group, int sub_m) {
@@ -1126,7 +1130,7 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
             return rc;
         }
         plan->smem = smem_bytes_for(plan->cta_group, plan->sub_m);
-        const void* sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32);
+        const void* sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, false);
         err = cudaFuncSetAttribute(sym, cudaFuncAttributeMaxDynamicSharedMemorySize, plan->smem);
         if (err == cudaSuccess && plan->cta_group == 2)
             err = cudaFuncSetAttribute(sym, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
@@ -1160,6 +1164,14 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
         plan->grid = clusters * plan->cta_group;
         if (stream_k_layout(p, slots, plan->sub_m)) {
             plan->grid = p.sk_groups * p.sk_lanes * plan->cta_group;
+            const void* sk_sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, true);
+            err = cudaFuncSetAttribute(sk_sym, cudaFuncAttributeMaxDynamicSharedMemorySize, plan->smem);
+            if (err == cudaSuccess && plan->cta_group == 2)
+                err = cudaFuncSetAttribute(sk_sym, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+            if (err != cudaSuccess) {
+                delete plan;
+                return cuda_fail("cudaFuncSetAttribute", err);
+            }
             if (const char* e = std::getenv("B200_TEST_DROP_PARTIAL_FLAGS")) p.sk_test_drop_flags = e[0] == '1';
         }
     }
@@ -1248,15 +1260,20 @@ static int plan_launch(B200Plan* plan, cudaStream_t stream) {
         ++cfg.numAttrs;
     }
     cudaError_t err;
-#define B200_LAUNCH(G, S, F) \
-    cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<G, S, F>, plan->tmA, plan->tmB, plan->tmD, plan->params, \
+#define B200_LAUNCH(G, S, F, K) \
+    cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<G, S, F, K>, plan->tmA, plan->tmB, plan->tmD, plan->params, \
                        plan->peer_maps)
-    if (plan->cta_group == 1)
-        err = plan->out_f32 ? B200_LAUNCH(1, 1, true) : B200_LAUNCH(1, 1, false);
+    const bool sk = plan->params.sk_iters > 0;
+    if (plan->cta_group == 1 && sk)
+        err = plan->out_f32 ? B200_LAUNCH(1, 1, true, true) : B200_LAUNCH(1, 1, false, true);
+    else if (plan->cta_group == 1)
+        err = plan->out_f32 ? B200_LAUNCH(1, 1, true, false) : B200_LAUNCH(1, 1, false, false);
     else if (plan->sub_m == 2)
-        err = plan->out_f32 ? B200_LAUNCH(2, 2, true) : B200_LAUNCH(2, 2, false);
+        err = plan->out_f32 ? B200_LAUNCH(2, 2, true, false) : B200_LAUNCH(2, 2, false, false);
+    else if (sk)
+        err = plan->out_f32 ? B200_LAUNCH(2, 1, true, true) : B200_LAUNCH(2, 1, false, true);
     else
-        err = plan->out_f32 ? B200_LAUNCH(2, 1, true) : B200_LAUNCH(2, 1, false);
+        err = plan->out_f32 ? B200_LAUNCH(2, 1, true, false) : B200_LAUNCH(2, 1, false, false);
 #undef B200_LAUNCH
     if (err != cudaSuccess) return cuda_fail("cudaLaunchKernelEx(gemm_tn_sm100_kernel)", err);
     return B200_OK;
@@ -1514,7 +1531,7 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
                                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != B200_OK) return rc;
     plan->smem = smem_bytes_for(plan->cta_group, plan->sub_m);
-    const void* sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32);
+    const void* sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, false);
     B200_CUDA_TRY(cudaFuncSetAttribute(sym, cudaFuncAttributeMaxDynamicSharedMemorySize, plan->smem));
     // One CTA (pair) per SM (pair); the persistent kernel needs no more.
     const int slots = plan->cta_group == 1 ? props.sm_count : props.sm_count / 2;
