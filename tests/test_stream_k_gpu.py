@@ -141,3 +141,29 @@ def test_stream_k_back_to_back_launches(monkeypatch):
     assert torch.equal(outs[0], outs[1])
     ref = a_d.double() @ b_d.double().T
     assert float((outs[0].double() - ref).abs().max()) <= 2.0 ** -20 * k
+
+
+def _random_cases(count=24, seed=2024):
+    import random
+    rng = random.Random(seed)
+    cases = []
+    while len(cases) < count:
+        mode = rng.choice(["1cta", "2cta"])
+        m = rng.randrange(64, 6144, 8)
+        n = rng.randrange(64, 4096, 8)
+        k = rng.randrange(64, 3072, 8)
+        cases.append((mode, (m, n, k)))
+    return cases
+
+
+@pytest.mark.parametrize("mode,shape", _random_cases())
+def test_stream_k_random_shapes(monkeypatch, mode, shape):
+    """Seeded random shapes, stream-K forced: every split layout the walk produces is exact
+    up to accumulation order (fp32 D within 2^-20 * K of the float64 product)."""
+    monkeypatch.setenv("B200_GEMM_SCHEDULE", "streamk")
+    m, n, k = shape
+    a, b = operands.uniform_operands(m, n, k, seed=m + n + k)
+    a_d, b_d = a.to(DEV), b.to(DEV)
+    d, _ = plan_run(a_d, b_d, torch.float32, mode, repeats=2)
+    ref = a_d.double() @ b_d.double().T
+    assert float((d.double() - ref).abs().max()) <= 2.0 ** -20 * k
