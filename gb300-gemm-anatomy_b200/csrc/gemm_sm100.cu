@@ -606,9 +606,10 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     // Consumed in this launch; the next launch's writers set them again.
                     for (int w = lane; w < nwriters; w += 32) p.sk_flags[slot_of(writer_cluster(w))] = 0;
                     if (stage_in_tmem) {
-                        // Four 32-column chunks (16 KB per warp) in flight per batch: the
-                        // loads are latency-bound, so their count in flight sets the speed.
-                        constexpr int kBatch = kCtaGroup == 2 ? 4 : 1;
+                        // One 32-column chunk per batch: this path only runs when no whole
+                        // tiles follow the split block (never under the auto policy, which
+                        // needs three waves), so it is kept small in registers.
+                        constexpr int kBatch = 1;
 #pragma unroll 1
                         for (int c0 = 0; c0 < kBN / 32; c0 += kBatch) {
                             uint32_t r[kBatch][32];
@@ -784,9 +785,10 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         if (role == 2) add_partial(c, packed);
                         store_chunk(c, packed);
                     }
-                } else if (role == 2) {
-                    // bf16 finisher: one 64-column chunk at a time (the partial sums
-                    // need the registers the drain-all path below keeps packed rows in).
+                } else if (kStreamK) {
+                    // bf16 under stream-K: one 64-column chunk at a time (the partial
+                    // sums need the registers the drain-all path below keeps packed
+                    // rows in).
 #pragma unroll 1
                     for (int c = 0; c < kChunks; ++c) {
                         uint32_t r0[32], r1[32], pk[32];
@@ -794,8 +796,10 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         tmem_ld_32x32b_x32(t_row + c * 64 + 32, r1);
                         tmem_ld_wait();
                         if (c == kChunks - 1) release_tmem();
-                        add_partial(2 * c, r0);
-                        add_partial(2 * c + 1, r1);
+                        if (role == 2) {
+                            add_partial(2 * c, r0);
+                            add_partial(2 * c + 1, r1);
+                        }
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
                             pk[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
