@@ -65,7 +65,7 @@ def profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling during the timed region."""
+    """SM clock and throttle-reason sampling during the timed region (NVML, else nvidia-smi)."""
 
     QUERY = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -77,7 +77,39 @@ class ClockSampler:
         self.lines = []
         self.t = None
 
+    def _nvml_handle(self):
+        """NVML handle of this process's CUDA device, matched by UUID (None if NVML is absent)."""
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid)
+        except Exception:  # noqa: BLE001 - any NVML problem falls back to nvidia-smi
+            return None
+
+    def _poll(self, nvml, handle):
+        stop = self.stop_event
+        while not stop.is_set():
+            try:
+                self.samples.append((time.time(),
+                                     nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM),
+                                     nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM),
+                                     nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)))
+            except Exception:  # noqa: BLE001
+                break
+            stop.wait(0.005)
+
     def start(self):
+        # NVML read every 5 ms (read-only queries); nvidia-smi as the fallback.
+        got = self._nvml_handle()
+        if got is not None:
+            self.stop_event = threading.Event()
+            self.samples = []
+            self.t = threading.Thread(target=self._poll, args=got, daemon=True)
+            self.nvml = got[0]
+            self.t.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
@@ -105,7 +137,33 @@ class ClockSampler:
         except ValueError:
             return None
 
+    def _stop_nvml(self):
+        self.stop_event.set()
+        self.t.join(timeout=2)
+        nvml = self.nvml
+        bits = {"hw_slowdown": nvml.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nvml.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nvml.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nvml.nvmlClocksEventReasonSwPowerCap}
+        lo, hi = getattr(self, "t_start", None), getattr(self, "t_end", None)
+        sm, mx, reasons = [], [], set()
+        for ts, clk, clk_max, mask in self.samples:
+            if lo is not None and hi is not None and not (lo <= ts <= hi):
+                continue
+            sm.append(float(clk))
+            mx.append(float(clk_max))
+            reasons.update(name for name, bit in bits.items() if mask & bit)
+        try:
+            nvml.nvmlShutdown()
+        except Exception:  # noqa: BLE001
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvml, 5 ms"}
+
     def stop(self):
+        if getattr(self, "nvml", None) is not None:
+            return self._stop_nvml()
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -135,7 +193,7 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 def cpu_reference_sample(a_cpu, b_cpu, budget_s: float):
