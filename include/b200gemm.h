@@ -224,13 +224,15 @@ int b200_gemm_plan_set_trace(B200Plan* plan, unsigned long long* trace, int64_t 
 int64_t b200_gemm_plan_launches(const B200Plan* plan);
 
 /* Tile schedule a plan runs. DYNAMIC: whole tiles handed out by a global
- * counter. STREAM_K: when the last wave of whole tiles would leave clusters
- * idle, the last tiles are split along K into equal runs per cluster, the
- * cut tiles finished through an fp32 partial buffer the plan allocates
- * (this ties each result's summation split to the device's SM count). The
- * environment variable B200_GEMM_SCHEDULE=dynamic|streamk overrides the
- * choice at plan creation. No counterpart in the reference, whose persistent
- * CuTe kernel (src/gemm/gemm_comparison.py candidate table) runs whole tiles.
+ * counter. STREAM_K (128x256 and 256x256 tiles only; chosen when the dynamic
+ * schedule would run at least three waves with the last one under 90 % busy):
+ * the leftover tiles are split along K into one equal run per cluster group
+ * and run first, whole tiles follow, and the cut tiles are finished through
+ * an fp32 partial buffer the plan allocates (this ties each result's
+ * summation split to the device's SM count). The environment variable
+ * B200_GEMM_SCHEDULE=dynamic|streamk overrides the choice at plan creation.
+ * No counterpart in the reference, whose persistent CuTe kernel
+ * (src/gemm/gemm_comparison.py candidate table) runs whole tiles.
  * Returns -1 for a NULL plan. */
 enum { B200_SCHEDULE_DYNAMIC = 0, B200_SCHEDULE_STREAM_K = 1 };
 int b200_gemm_plan_schedule(const B200Plan* plan);
