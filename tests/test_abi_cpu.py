@@ -111,3 +111,38 @@ def test_shard_range_partitions(n, world, granule):
     for b, e in ranges:
         assert b <= e and (b % granule == 0 or b == n)
     assert _lib.shard_range(128256, 8, 0, 16) == (0, 16032)
+
+
+_C_CALLER = r"""
+#include <stdio.h>
+#include "b200gemm.h"
+
+int main(void) {
+    B200Plan* plan = NULL;
+    if (b200_abi_version() != B200_ABI_VERSION) return 1;
+    if (b200_plan_info_size() != sizeof(B200PlanInfo)) return 2;
+    if (b200_gemm_supported(8192, 8192, 8192, 8192, B200_OUT_BF16, B200_MODE_AUTO) != B200_OK) return 3;
+    if (b200_gemm_supported(64, 64, 60, 64, B200_OUT_BF16, B200_MODE_AUTO) != B200_ERR_UNSUPPORTED) return 4;
+    if (b200_gemm_plan_schedule(NULL) != -1) return 5;
+    if (b200_gemm_plan_create_ex(64, 64, 64, NULL, NULL, NULL, 64, B200_OUT_BF16, B200_MODE_AUTO,
+                                 NULL, &plan, NULL) != B200_ERR_INVALID_ARGUMENT) return 6;
+    if (plan != NULL) return 7;
+    printf("%s\n", b200_last_error());
+    return 0;
+}
+"""
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """A C99 caller compiles against include/b200gemm.h with warnings as errors, links
+    against the library and gets the handshake and argument checks without a GPU."""
+    src = tmp_path / "caller.c"
+    src.write_text(_C_CALLER)
+    exe = tmp_path / "caller"
+    libdir = _lib.LIB_PATH.parent
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-I", str(HEADER.parent),
+                    str(src), "-o", str(exe), f"-L{libdir}", "-l:" + _lib.LIB_PATH.name,
+                    f"-Wl,-rpath,{libdir}"], check=True, capture_output=True, text=True)
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert res.returncode == 0, (res.returncode, res.stdout, res.stderr)
+    assert "device pointer" in res.stdout  # the thread-local message of the last failed call
