@@ -271,6 +271,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--mode", choices=["auto", "1cta", "2cta", "2cta_m512"], default="auto")
+    ap.add_argument("--schedule", choices=["auto", "dynamic", "streamk"], default="auto",
+                    help="tile schedule (auto: the library's choice)")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -280,6 +282,8 @@ def main() -> int:
         return 2
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.schedule != "auto":
+        os.environ["B200_GEMM_SCHEDULE"] = args.schedule  # read at plan creation
 
     import torch
     import torch.distributed as dist
@@ -307,6 +311,7 @@ def main() -> int:
     stream = torch.cuda.current_stream(dev)
     plan = G.GemmPlan(a, b, out, mode=args.mode, stream=stream)
     launches_per_step = plan.launches_per_execute
+    schedule = plan.schedule
 
     for _ in range(args.warmup):
         plan.execute()
@@ -411,7 +416,7 @@ def main() -> int:
             "data": "synthetic: A,B ~ N(0,1)*0.1 bf16 (seed 1; shard r>0 seed 1000+r)",
             "config": {"workload": f"gemm_tn {M}x{N * world}x{K} bf16->bf16, N-sharded "
                                    f"{N} cols/GPU" if world > 1 else f"gemm_tn {M}x{N}x{K} bf16->bf16",
-                       "m": M, "n_per_gpu": N, "k": K, "mode": args.mode,
+                       "m": M, "n_per_gpu": N, "k": K, "mode": args.mode, "schedule": schedule,
                        "parallelism": f"n-shard x{world}", "l2": "inputs 256 MiB > L2, no flush"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
                          "frac": achieved / peak, "peak_kind": f"{peaks_kind} burst bf16",

@@ -119,6 +119,8 @@ def build_arg_parser() -> argparse.ArgumentParser:
                         "persistent_2cta_m512, "
                         "torch_matmul, "
                         "heuristic_first_supported (the reference's cuBLASLt bridge)")
+    p.add_argument("--schedule", choices=("auto", "dynamic", "streamk"), default="auto",
+                   help="tile schedule of the B200 candidates (auto: the library's choice)")
     p.add_argument("--peak-tflops", type=float, default=None,
                    help="roofline denominator (default: MEASURED_PEAKS.json bf16_tflops)")
     return p
@@ -417,6 +419,9 @@ def main(argv=None) -> int:
         return 2 if exc.code else 0
     if args.self_test:
         return run_self_test()
+    if args.schedule != "auto":
+        import os
+        os.environ["B200_GEMM_SCHEDULE"] = args.schedule  # read at plan creation
     try:
         select_candidates(args.candidates)
         text = execute_measurement(args)

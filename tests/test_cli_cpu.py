@@ -23,7 +23,7 @@ def test_gemm_comparison_self_test():
 
 @pytest.mark.parametrize("args", [["--iterations", "0"], ["--iterations", "101"],
                                   ["--warmup-iterations", "abc"], ["--shape", "8x8"],
-                                  ["--candidates", "nope"]])
+                                  ["--candidates", "nope"], ["--schedule", "fast"]])
 def test_gemm_comparison_usage_errors(args):
     r = run("b200gemm.cli.gemm_comparison", *args)
     assert r.returncode == 2 and r.stdout == ""
@@ -88,3 +88,13 @@ def test_ncu_bridge_usage():
     assert run("b200gemm.cli.ncu_bridge", "--kind", "memory").returncode == 2
     r = run("b200gemm.cli.ncu_bridge", "--kind", "memory", "--kernel", "x", "--", "true")
     assert r.returncode == 2  # memory kind needs --useful-bytes
+
+
+def test_schedule_options_parse():
+    from b200gemm.cli import gemm_comparison
+    p = gemm_comparison.build_arg_parser()
+    assert p.parse_args([]).schedule == "auto"
+    assert p.parse_args(["--schedule", "streamk"]).schedule == "streamk"
+    r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--schedule", "sometimes"],
+                       capture_output=True, text=True, timeout=120)
+    assert r.returncode == 2 and "--schedule" in r.stderr
