@@ -1013,6 +1013,15 @@ static void raster_for(const GemmParams& p, int tile_m, int sub_m, int* group, i
     g = std::max(2, std::min(16, g));
     *group = std::min(g, std::max(p.num_m_blocks, 1));
     *raster_n = 0;
+    // A B that stays in L2 (<= 64 MiB) and is the narrower side: walk every
+    // n-block of one m-block before the next, so A and B each cross HBM once.
+    // Measured on B200 (bf16 D): 8192 x {1792, 2048, 4096} x 4096 and
+    // 8192 x 3072 x 8192 run 2.7-4 % faster than with m-groups.
+    const double b_bytes = 2.0 * static_cast<double>(p.n) * static_cast<double>(p.k);
+    if (p.num_n_blocks < p.num_m_blocks && b_bytes <= 64.0 * 1024 * 1024) {
+        *raster_n = 1;
+        *group = std::max(p.num_n_blocks, 1);
+    }
     if (const char* e = std::getenv("B200_GEMM_GROUP")) {
         const int v = std::atoi(e);
         if (v >= 1 && v <= 4096) *group = v;
