@@ -88,6 +88,14 @@ PlanInfo = _i64_struct(
     doubles=["waves", "flop_count"],
 )
 
+PolicyInfo = _i64_struct(
+    "B200PolicyInfo",
+    ["mode", "tile_m", "tile_n", "num_m_blocks", "num_n_blocks", "num_k_blocks", "num_tiles",
+     "clusters", "raster_n", "group", "schedule", "sk_groups", "sk_lanes", "sk_lane_n",
+     "sk_rounds", "sk_split_tiles", "grid_ctas"],
+    doubles=["waves"],
+)
+
 StreamConfig = _i64_struct(
     "B200StreamConfig", ["method", "stages", "stage_bytes", "ctas_per_sm", "passes", "rotation"]
 )
@@ -126,6 +134,8 @@ SIGNATURES = {
     "b200_gemm": (_INT, [_I64, _I64, _I64, _P, _P, _P, _I64, _INT, _INT, _P]),
     "b200_gemm_plan_launches": (_I64, [_P]),
     "b200_gemm_plan_schedule": (_INT, [_P]),
+    "b200_policy_info_size": (ctypes.c_size_t, []),
+    "b200_gemm_policy": (_INT, [_I64, _I64, _I64, _INT, _INT, ctypes.POINTER(PolicyInfo)]),
     "b200_gemm_plan_set_trace": (_INT, [_P, _P, _I64]),
     "b200_gemm_plan_set_peers": (_INT, [_P, _INT, ctypes.POINTER(_P)]),
     "b200_ipc_handle_size": (ctypes.c_size_t, []),
@@ -151,6 +161,7 @@ _STRUCT_SIZES = {
     "b200_plan_info_size": PlanInfo,
     "b200_device_info_size": DeviceInfo,
     "b200_stream_result_size": StreamResult,
+    "b200_policy_info_size": PolicyInfo,
 }
 
 _lib = None

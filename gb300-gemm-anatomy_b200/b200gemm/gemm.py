@@ -198,3 +198,22 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, *,
     finally:
         plan.destroy()
     return out
+
+
+_MODE_NAME = {v: k for k, v in _MODE_CODE.items()}
+
+
+def policy(m: int, n: int, k: int, *, mode: str = "auto", sm_count: int = 148) -> dict:
+    """The plan's host-side choices for an M x N x K GEMM on a GPU with ``sm_count`` SMs,
+    computed without a device (b200_gemm_policy): resolved mode, tile grid, raster,
+    schedule (and the stream-K layout when it applies)."""
+    lib = _lib.load()
+    if mode not in _MODE_CODE:
+        raise ValueError(f"mode must be one of {sorted(_MODE_CODE)}")
+    info = _lib.PolicyInfo()
+    _lib.check(lib.b200_gemm_policy(m, n, k, _MODE_CODE[mode], sm_count, ctypes.byref(info)),
+               "b200_gemm_policy", lib)
+    out = {name: getattr(info, name) for name, _ in info._fields_}
+    out["mode"] = _MODE_NAME[out["mode"]]
+    out["schedule"] = "stream_k" if out["schedule"] == 1 else "dynamic"
+    return out

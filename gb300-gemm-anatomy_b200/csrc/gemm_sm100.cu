@@ -1431,6 +1431,65 @@ int b200_gemm_plan_schedule(const B200Plan* plan) {
     return plan->params.sk_iters > 0 ? B200_SCHEDULE_STREAM_K : B200_SCHEDULE_DYNAMIC;
 }
 
+size_t b200_policy_info_size(void) { return sizeof(B200PolicyInfo); }
+
+int b200_gemm_policy(int64_t m, int64_t n, int64_t k, int mode, int sm_count, B200PolicyInfo* out) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    if (out == nullptr || sm_count < 2) {
+        b200::set_error("policy: out must not be NULL and sm_count must be at least 2");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (m < 1 || n < 1 || k < 1) {
+        b200::set_error("policy: (M,N,K)=(%lld,%lld,%lld) must be positive", (long long)m, (long long)n,
+                        (long long)k);
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    const int rc = b200::check_shape(m, n, k, n + (8 - n % 8) % 8, B200_OUT_BF16, mode);
+    if (rc != B200_OK) return rc;
+    // The same steps as plan creation, with the resident clusters a full GPU holds.
+    const int resolved = b200::resolve_mode(mode, m, n, sm_count);
+    const int cta_group = resolved == B200_MODE_1CTA ? 1 : 2;
+    const int sub_m = resolved == B200_MODE_2CTA_M512 ? 2 : 1;
+    const int tile_m = b200::kRowsPerCta * sub_m * cta_group;
+    b200::GemmParams p{};
+    p.m = static_cast<int>(m);
+    p.n = static_cast<int>(n);
+    p.k = static_cast<int>(k);
+    p.num_m_blocks = static_cast<int>((m + tile_m - 1) / tile_m);
+    p.num_n_blocks = static_cast<int>((n + b200::kBN - 1) / b200::kBN);
+    p.num_k_blocks = static_cast<int>((k + b200::kBK - 1) / b200::kBK);
+    p.num_tiles = p.num_m_blocks * p.num_n_blocks;
+    b200::raster_for(p, tile_m, sub_m, &p.group_m, &p.raster_n);
+    const int slots = cta_group == 1 ? sm_count : sm_count / 2;
+    const int clusters = std::min(p.num_tiles, slots);
+    int grid = clusters * cta_group;
+    const bool sk = b200::stream_k_layout(p, slots, sub_m);
+    if (sk) grid = p.sk_groups * p.sk_lanes * cta_group;
+    B200PolicyInfo& o = *out;
+    std::memset(&o, 0, sizeof(o));
+    o.mode = resolved;
+    o.tile_m = tile_m;
+    o.tile_n = b200::kBN;
+    o.num_m_blocks = p.num_m_blocks;
+    o.num_n_blocks = p.num_n_blocks;
+    o.num_k_blocks = p.num_k_blocks;
+    o.num_tiles = p.num_tiles;
+    o.clusters = sk ? p.sk_groups * p.sk_lanes : clusters;
+    o.raster_n = p.raster_n;
+    o.group = p.group_m;
+    o.schedule = sk ? B200_SCHEDULE_STREAM_K : B200_SCHEDULE_DYNAMIC;
+    o.sk_groups = p.sk_groups;
+    o.sk_lanes = p.sk_lanes;
+    o.sk_lane_n = p.sk_lane_n;
+    o.sk_rounds = p.sk_rounds;
+    o.sk_split_tiles = sk ? p.sk_iters / p.num_k_blocks : 0;
+    o.grid_ctas = grid;
+    o.waves = static_cast<double>(p.num_tiles) / slots;
+    return B200_OK;
+    B200_ABI_GUARD_END
+}
+
 int64_t b200_gemm_plan_launches(const B200Plan* plan) {
     if (plan == nullptr || plan->empty_problem) return 0;
     return 1;

@@ -237,6 +237,36 @@ int64_t b200_gemm_plan_launches(const B200Plan* plan);
 enum { B200_SCHEDULE_DYNAMIC = 0, B200_SCHEDULE_STREAM_K = 1 };
 int b200_gemm_plan_schedule(const B200Plan* plan);
 
+/* Host-side policy of a GEMM plan, computed without a device: the mode that
+ * B200_MODE_AUTO resolves to, the tile grid, the raster of the tile walk and
+ * the tile schedule, for a GPU with `sm_count` SMs on which one cluster per
+ * SM (1-CTA) or per SM pair (2-CTA) is resident. Plans on such a GPU make the
+ * same choices; the environment overrides B200_GEMM_SCHEDULE, B200_GEMM_RASTER
+ * and B200_GEMM_GROUP apply here as well. No counterpart in the reference. */
+typedef struct B200PolicyInfo {
+    int64_t mode;            /* resolved B200_MODE_1CTA, _2CTA or _2CTA_M512 */
+    int64_t tile_m;          /* rows of D per tile (per CTA pair in 2-CTA modes) */
+    int64_t tile_n;
+    int64_t num_m_blocks;
+    int64_t num_n_blocks;
+    int64_t num_k_blocks;    /* 64-wide k-slices */
+    int64_t num_tiles;
+    int64_t clusters;        /* resident clusters assumed */
+    int64_t raster_n;        /* 0: groups of m-blocks walk every n-block; 1: the reverse */
+    int64_t group;           /* blocks per raster group */
+    int64_t schedule;        /* B200_SCHEDULE_* */
+    int64_t sk_groups;       /* stream-K: cluster groups, lanes per group, lane axis */
+    int64_t sk_lanes;
+    int64_t sk_lane_n;
+    int64_t sk_rounds;       /* whole-tile rounds after the split block */
+    int64_t sk_split_tiles;  /* super-tiles in the split block */
+    int64_t grid_ctas;
+    double waves;            /* num_tiles / clusters */
+} B200PolicyInfo;
+
+size_t b200_policy_info_size(void);
+int b200_gemm_policy(int64_t m, int64_t n, int64_t k, int mode, int sm_count, B200PolicyInfo* out);
+
 /* ------------------------------------------------------------------------ */
 /* Memory path: global -> shared streaming (LDGSTS / TMA)                     */
 /* Replaces the ldgsts and tma benchmark binaries                             */

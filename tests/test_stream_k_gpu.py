@@ -167,3 +167,25 @@ def test_stream_k_random_shapes(monkeypatch, mode, shape):
     d, _ = plan_run(a_d, b_d, torch.float32, mode, repeats=2)
     ref = a_d.double() @ b_d.double().T
     assert float((d.double() - ref).abs().max()) <= 2.0 ** -20 * k
+
+
+@pytest.mark.parametrize("shape", [(8192, 8192, 8192), (4096, 4096, 4096), (16384, 512, 4096),
+                                   (32768, 512, 4096), (512, 512, 512), (8192, 1792, 4096),
+                                   (8192, 4096, 4096)])
+def test_policy_preview_matches_plans(shape):
+    """b200_gemm_policy (no device) predicts what plan creation on this GPU decides."""
+    m, n, k = shape
+    sm = torch.cuda.get_device_properties(0).multi_processor_count
+    pred = G.policy(m, n, k, sm_count=sm)
+    a = torch.empty((m, k), dtype=torch.bfloat16, device=DEV)
+    b = torch.empty((n, k), dtype=torch.bfloat16, device=DEV)
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=DEV)
+    plan = G.GemmPlan(a, b, out)
+    try:
+        info = plan.info
+        assert pred["schedule"] == plan.schedule
+        assert pred["num_tiles"] == info["num_tiles"]
+        assert pred["grid_ctas"] == info["grid_ctas"]
+        assert pred["tile_m"] == info["tile_m"]
+    finally:
+        plan.destroy()
