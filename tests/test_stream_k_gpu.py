@@ -56,6 +56,9 @@ CASES = [
     ("2cta", (5000, 2104, 200)),       # 180 tiles, ragged, 4 k-slices
     ("2cta", (16384, 512, 4096)),      # the reference's skinny frozen shape
     ("2cta", (512, 16384, 4096)),      # and its transpose
+    ("2cta", (2304, 2304, 8)),         # one k-slice: some groups get no run at all
+    ("2cta", (2304, 2304, 72)),        # two k-slices
+    ("1cta", (4096, 512, 64)),         # lanes with a single k-slice
 ]
 
 
