@@ -101,8 +101,9 @@ class ClockSampler:
             stop.wait(0.005)
 
     def start(self):
-        # NVML read every 5 ms (read-only queries); nvidia-smi as the fallback.
-        got = self._nvml_handle()
+        # NVML read every 5 ms (read-only queries); nvidia-smi as the fallback
+        # (or when B200_BENCH_CLOCKS=smi).
+        got = None if os.environ.get("B200_BENCH_CLOCKS") == "smi" else self._nvml_handle()
         if got is not None:
             self.stop_event = threading.Event()
             self.samples = []
