@@ -17,6 +17,21 @@ operands copied from pinned host memory and D copied back every step.
 "mkl,nkl->mnl", src/gemm/gemm_comparison.py:2705-2722) on a row slab of the
 same operands using all host threads. `--impl reference` times that CPU path
 alone as the reference arm.
+
+Further sections of the same JSON line (after the headline's timed region;
+`--no-extras` skips them):
+  llm_shard    (every N) config c5, 8192 x {128256, 14336} x 4096, N split over
+               the ranks (strong scaling), gathers none / fused / nccl, each
+               checked on every rank against torch IEEE fp32 on 64 sampled rows
+               before it is timed (max over ranks)
+  sustained    (N=1) >= 2 s windows of back-to-back 8192^3 launches, ours and
+               cuBLAS alternated, median SM clock and power per window (NVML),
+               frac against the measured sustained bf16 peak
+  memory_path  (N=1) config c2: 4 GiB streamed by TMA and LDGSTS, device
+               checksum == host checksum, GB/s against the measured HBM copy
+               peak, and the CPU streaming-checksum baseline on all host cores
+  umma         (N=1) config c3: 2-SM tcgen05.mma N=256 depth 256 on all SMs,
+               exact known answer, FLOP/cycle/SM
 """
 from __future__ import annotations
 
@@ -95,7 +110,8 @@ class ClockSampler:
                 self.samples.append((time.time(),
                                      nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM),
                                      nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM),
-                                     nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)))
+                                     nvml.nvmlDeviceGetCurrentClocksEventReasons(handle),
+                                     nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0))
             except Exception:  # noqa: BLE001
                 break
             stop.wait(0.005)
@@ -138,6 +154,23 @@ class ClockSampler:
         except ValueError:
             return None
 
+    def window(self, lo: float, hi: float):
+        """Median SM clock, median power and throttle reasons of the NVML samples in [lo, hi]."""
+        nvml = self.nvml
+        bits = {"hw_slowdown": nvml.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nvml.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nvml.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nvml.nvmlClocksEventReasonSwPowerCap}
+        sm, pw, reasons = [], [], set()
+        for ts, clk, _, mask, watts in list(self.samples):
+            if lo <= ts <= hi:
+                sm.append(float(clk))
+                pw.append(float(watts))
+                reasons.update(name for name, bit in bits.items() if mask & bit)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "power_w": statistics.median(pw) if pw else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
     def _stop_nvml(self):
         self.stop_event.set()
         self.t.join(timeout=2)
@@ -148,7 +181,7 @@ class ClockSampler:
                 "sw_power_cap": nvml.nvmlClocksEventReasonSwPowerCap}
         lo, hi = getattr(self, "t_start", None), getattr(self, "t_end", None)
         sm, mx, reasons = [], [], set()
-        for ts, clk, clk_max, mask in self.samples:
+        for ts, clk, clk_max, mask, _ in self.samples:
             if lo is not None and hi is not None and not (lo <= ts <= hi):
                 continue
             sm.append(float(clk))
@@ -224,6 +257,223 @@ def cpu_reference_sample(a_cpu, b_cpu, budget_s: float):
     return flop / dt / 1e12, threads, rows * reps, dt
 
 
+def _event_ms(fn, iters, stream):
+    """CUDA-event time of `iters` back-to-back calls of fn() on `stream`, in ms per call."""
+    import torch
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def sustained_section(plan, a, b, local, peaks, seconds: float = 2.0):
+    """Back-to-back 8192^3 launches for `seconds` each, ours and cuBLAS alternated
+    twice, with NVML clock and power over each window: steady operation under
+    the 1000 W cap rather than the short headline burst."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    flop = 2.0 * a.shape[0] * b.shape[0] * a.shape[1]
+    c = torch.empty((a.shape[0], b.shape[0]), dtype=torch.bfloat16, device=a.device)
+    bt = b.t()
+    impls = {"b200": plan.execute, "cublas": lambda: torch.mm(a, bt, out=c)}
+    per_launch = {}
+    for name, fn in impls.items():  # launches per window from a short probe
+        fn()
+        per_launch[name] = _event_ms(fn, 20, stream)
+    sampler = ClockSampler(local)
+    sampler.start()
+    has_nvml = getattr(sampler, "nvml", None) is not None
+    time.sleep(0.2)
+    runs = {"b200": [], "cublas": []}
+    for _ in range(2):
+        for name, fn in impls.items():
+            n = max(1, int(seconds * 1e3 / per_launch[name]))
+            torch.cuda.synchronize()
+            t0 = time.time()
+            ms = _event_ms(fn, n, stream)
+            t1 = time.time()
+            win = sampler.window(t0, t1) if has_nvml else {}
+            runs[name].append({"tflops": flop / (ms / 1e3) / 1e12, "launches": n,
+                               "seconds": n * ms / 1e3, **win})
+    sampler.stop()
+    plan.synchronize()
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    out = {"workload": "gemm_tn 8192x8192x8192 bf16->bf16, back to back", "unit": UNIT,
+           "peak": peak, "peak_kind": "bf16_tflops_sustained"}
+    for name, rs in runs.items():
+        v = statistics.median(r["tflops"] for r in rs)
+        out[name] = {"tflops": v, "frac": v / peak, "windows": rs}
+    if has_nvml:
+        for name in runs:
+            pw = [r["power_w"] for r in runs[name] if r.get("power_w")]
+            if pw:
+                out[name]["tflops_per_joule"] = out[name]["tflops"] / statistics.median(pw)
+    return out
+
+
+def llm_shard_section(world, rank, dev, shapes=((128256, 4096), (14336, 4096)), m=8192,
+                      iters=10, warmup=3):
+    """Config c5 N-sharded over the ranks (strong scaling: N fixed, split by
+    b200_shard_range), each gather timed: none (the shard GEMM alone), fused
+    (the GEMM epilogue stores every output chunk into every rank's full D over
+    NVLink) and nccl (GEMM, then NCCL all-gather + re-layout). Before timing,
+    every rank checks the full gathered D (its own shard with gather none) on
+    64 sampled rows against torch's IEEE fp32 matmul with the bf16 rule;
+    the results are combined over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from b200gemm import check, dist as bdist, operands
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    gathers = ("none", "fused", "nccl") if world > 1 else ("none",)
+    out = {"operands": "c5: A ~ N(0,1), B ~ N(0,0.02), seed 2, drawn on the device",
+           "scaling": "strong: N fixed, split over the ranks", "check_rows": 64, "shapes": {}}
+    for (n, k) in shapes:
+        a, b_full = operands.llm_operands_device(n, k, dev, m=m)
+        n0, n1 = bdist.shard_bounds(n, world, rank)
+        b = b_full[n0:n1].contiguous()
+        rows = torch.arange(0, m, m // 64, device=dev)
+        ref = a[rows].float() @ b_full.float().t()
+        amax, bmax = float(a.float().abs().max()), float(b_full.float().abs().max())
+        del b_full
+        res = {"shard_cols": n1 - n0}
+        for gather in gathers:
+            sg = bdist.ShardedGemm(a, b, n, p2p=(gather == "fused"))
+            mode = "none" if gather == "none" else "full"
+            got = sg.run(mode)
+            torch.cuda.synchronize()
+            want = ref if gather != "none" else ref[:, n0:n1]
+            ok = 1
+            try:
+                check.bf16_tolerance_check(f"{m}x{n}x{k} {gather}", want, got[rows].float(), k, amax, bmax)
+            except check.CorrectnessError as exc:
+                print(f"bench.py: llm_shard check failed on rank {rank}: {exc}", file=sys.stderr)
+                ok = 0
+            del got
+            for _ in range(warmup):
+                sg.run(mode)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            ms = _event_ms(lambda: sg.run(mode), iters, torch.cuda.current_stream())
+            sg.synchronize()
+            t = torch.tensor([ms, -ok], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)  # slowest rank; any failed check
+            sg.destroy()
+            ms = float(t[0])
+            entry = {"ms": ms, "tflops": 2.0 * m * n * k / (ms / 1e3) / 1e12,
+                     "check": "pass" if float(t[1]) < 0 else "FAIL"}
+            if gather != "none":
+                sent = m * (n1 - n0) * 2 * (world - 1)
+                entry["sent_gbps_per_gpu"] = sent / (ms / 1e3) / 1e9
+            res[gather] = entry
+            torch.cuda.empty_cache()
+        out["shapes"][f"{m}x{n}x{k}"] = res
+        del a, b, ref
+        torch.cuda.empty_cache()
+    return out
+
+
+def _parallel_checksum(words, threads):
+    """XOR and 64-bit sum of a uint32 array on `threads` host threads (numpy
+    reductions release the GIL)."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+
+    parts = np.array_split(words, threads * 4)
+
+    def one(w):
+        return int(np.bitwise_xor.reduce(w)) if w.size else 0, int(w.sum(dtype=np.uint64))
+
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        res = list(pool.map(one, parts))
+    x = 0
+    tot = 0
+    for px, ps in res:
+        x ^= px
+        tot = (tot + ps) & ((1 << 64) - 1)
+    return x, tot
+
+
+def memory_path_section(dev, peaks, nbytes=4 << 30, reps=5):
+    """Config c2: a 4 GiB seeded bf16 buffer streamed HBM -> SMEM by TMA and by
+    LDGSTS (best configurations of the sweep, and the best of the reference's
+    1-CTA/SM grid). Each first checksums the buffer on the device (must equal
+    the host checksum bit for bit), then is timed in the reference's sink mode:
+    GB/s = working set / kernel time (src/memory/ldgsts.cu:898,913-916). The CPU
+    baseline streams the same bytes through an XOR + 64-bit sum on all host cores."""
+    import argparse as _ap
+
+    import numpy as np
+    import torch
+
+    from b200gemm.cli import memory_paths as cmp
+
+    g = torch.Generator(device=dev).manual_seed(2)
+    buf = torch.empty(nbytes // 2, dtype=torch.bfloat16, device=dev)
+    chunk = 1 << 28
+    for i in range(0, buf.numel(), chunk):
+        buf[i:i + chunk] = torch.rand(min(chunk, buf.numel() - i), generator=g, device=dev) * 2 - 1
+    words = buf.view(torch.int32).cpu().numpy().view(np.uint32)
+    threads = os.cpu_count() or 1
+    _parallel_checksum(words[: 1 << 24], threads)  # warm the pool
+    cpu_times, host = [], None
+    for _ in range(3):
+        t0 = time.perf_counter()
+        host = _parallel_checksum(words, threads)
+        cpu_times.append(time.perf_counter() - t0)
+    cmp._HOST_CHECKSUMS[(buf.data_ptr(), nbytes)] = host
+    del words
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    args = _ap.Namespace(fill="uniform", warmup_ms=100, repetitions=reps, passes=1,
+                         run_kind="benchmark")
+    configs = [("best_tma", "tma_sw128", 2, 16384, 4), ("best_ldgsts", "ldgsts", 2, 16384, 4),
+               ("ref_grid_tma", "tma", 2, 32768, 1), ("ref_grid_ldgsts", "ldgsts", 2, 32768, 1)]
+    out = {"workload": f"{nbytes >> 30} GiB seeded uniform bf16, HBM -> SMEM, 1 pass", "unit": "GB/s",
+           "peak": hbm, "peak_kind": "hbm_gbs (measured copy)"}
+    for label, method, stages, sb, ctas in configs:
+        rows = cmp.run_one(buf, method, stages, sb, ctas, args, nbytes, hbm)
+        gbps = [r["effective_gbps"] for r in rows]
+        out[label] = {"method": method, "stages": stages, "stage_bytes": sb, "ctas_per_sm": ctas,
+                      "gbps_best": max(gbps), "gbps_median": statistics.median(gbps),
+                      "frac": max(gbps) / hbm, "checksum": "device == host",
+                      "checksum_xor": rows[0]["checksum_xor"], "checksum_sum": rows[0]["checksum_sum"]}
+    out["cpu_baseline"] = {"gbps": nbytes / min(cpu_times) / 1e9, "unit": "GB/s", "cores": threads,
+                           "kind": "XOR + 64-bit sum of every 32-bit word, numpy on host threads",
+                           "sample": f"the same {nbytes >> 30} GiB, best of 3"}
+    del buf
+    torch.cuda.empty_cache()
+    return out
+
+
+def umma_section(reps=5):
+    """Config c3: tcgen05.mma 2-SM (cta_group::2), M=256 N=256 K=16, depth 256,
+    one CTA pair on every SM pair, 1000 commit rounds; the integer known answer
+    is checked exactly first (src/compute/umma_1sm.cu:577-586, 1164-1167)."""
+    import argparse as _ap
+
+    import torch
+
+    from b200gemm.cli import umma as cu
+
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    args = _ap.Namespace(operands="pattern", iterations=1000, warmup=3, repetitions=reps,
+                         self_test=False)
+    rows = cu.run_case(2, 256, 256, args, sms // 2, sms, "umma_2sm")
+    fpc = [r["flops_per_cycle_per_sm"] for r in rows]
+    tf = [r["tflops"] for r in rows]
+    return {"workload": "umma_2sm N=256 depth=256 x 1000 iterations, all SMs", "check": "exact",
+            "flops_per_cycle_per_sm": statistics.median(fpc), "ceiling_flops_per_cycle_per_sm": 8192,
+            "frac": statistics.median(fpc) / 8192, "tflops_all_sms": statistics.median(tf)}
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -277,6 +527,10 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the llm_shard, sustained, memory_path and umma sections")
+    ap.add_argument("--sustained-s", type=float, default=2.0,
+                    help="seconds per window of the sustained section (two windows per impl)")
     args = ap.parse_args()
     if args.warmup < 3:
         print("bench.py: --warmup must be >= 3", file=sys.stderr)
@@ -398,8 +652,23 @@ def main() -> int:
     e2e = {"value": flop_per_gpu * world / (e2e_ms / 1e3) / 1e12, "unit": UNIT,
            "h2d_bytes_per_step": (a.numel() + b.numel()) * 2, "d2h_bytes_per_step": out.numel() * 2,
            "ms_per_step": e2e_ms, "pipelined": "H2D / GEMM / D2H on three streams"}
-    for pl in plans:
+    for pl in plans[1:]:
         pl.destroy()
+    del bufs, plans, a_pin, b_pin, d_pin
+
+    extras = {}
+    if not args.no_extras:
+        if world == 1:
+            extras["sustained"] = sustained_section(plan, a, b, local, peaks, args.sustained_s)
+        plan.destroy()
+        del a, b, out
+        torch.cuda.empty_cache()
+        extras["llm_shard"] = llm_shard_section(world, rank, dev)
+        if world == 1:
+            extras["memory_path"] = memory_path_section(dev, peaks)
+            extras["umma"] = umma_section()
+    else:
+        plan.destroy()
 
     if rank == 0:
         cpu = None
@@ -426,6 +695,7 @@ def main() -> int:
             "e2e": e2e,
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks,
+            **extras,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -153,6 +153,7 @@ SIGNATURES = {
     "b200_stream_plan_destroy": (_INT, [_P]),
     "b200_umma_probe": (_INT, [ctypes.POINTER(UmmaConfig), _P, _P, _P, _P, _P, _P]),
     "b200_selftest_bounded_wait": (_INT, [ctypes.c_ulonglong, _P, _P]),
+    "b200_selftest_occupy": (_INT, [_INT, _INT, ctypes.c_ulonglong, _P]),
     "b200_shard_range": (_INT, [_I64, _I64, _I64, _I64, ctypes.POINTER(_I64),
                                 ctypes.POINTER(_I64)]),
 }

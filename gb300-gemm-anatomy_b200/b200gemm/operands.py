@@ -62,6 +62,25 @@ def llm_operands(n: int, k: int, m: int = LLM_M, seed: int = 2):
     return normal_operands(m, n, k, seed, 1.0, 0.02)
 
 
+def llm_operands_device(n: int, k: int, device, m: int = LLM_M, seed: int = 2):
+    """Config c5 drawn on the GPU: A ~ N(0,1) (M x K) then B ~ N(0, 0.02) (N x K),
+    fp32 from a device ``torch.Generator`` seeded with `seed`, cast to bf16.
+
+    Same distributions, shapes and draw order as ``llm_operands``; drawing on the
+    device keeps the 128256 x 4096 weight matrix from costing every rank of a
+    multi-GPU run ~20 s of host time. Every rank with the same seed and GPU
+    model draws the same values.
+    """
+    g = torch.Generator(device=device).manual_seed(seed)
+    a = (torch.randn((m, k), generator=g, device=device) * 1.0).to(torch.bfloat16)
+    b = torch.empty((n, k), dtype=torch.bfloat16, device=device)
+    step = max(1, (1 << 28) // max(k, 1))  # rows per fp32 draw (<= 1 GiB of fp32 at a time)
+    for r in range(0, n, step):
+        rows = min(step, n - r)
+        b[r:r + rows] = (torch.randn((rows, k), generator=g, device=device) * 0.02).to(torch.bfloat16)
+    return a, b
+
+
 def ref_compat_available() -> bool:
     try:
         import cutlass  # noqa: F401

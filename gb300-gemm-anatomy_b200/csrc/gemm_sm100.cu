@@ -113,11 +113,11 @@ struct GemmParams {
     // then `sk_rounds` rounds of whole super-tiles follow (split + j *
     // sk_groups + g in round j), so every group ends at the same time on whole
     // tiles and the reductions of the cut tiles overlap the later MMAs. A cut
-    // super-tile is finished by the group that runs its first k-slices (that
-    // group's last run) after every later group holding a run of it (their
-    // first run) has left its fp32 partial in its own slot of sk_partial and
-    // set its sk_flags word; the finisher adds the partials in k order, writes
-    // D and clears the flags.
+    // super-tile is finished by the group that runs its last k-slices (that
+    // group's last split-block run) after every earlier group holding a run of
+    // it (their first run) has left its fp32 partial in its own slot of
+    // sk_partial and set its sk_flags word; the finisher adds the partials in
+    // k order, writes D and clears the flags.
     int sk_rounds;
     int sk_groups;
     int sk_lanes;
@@ -147,16 +147,16 @@ __device__ __forceinline__ void trace_stamp(const GemmParams& p, int slot) {
 }
 
 // One unit of a cluster's work: super-tile t over k-slices [kb0, kb1).
-// role 0: the whole K range; 1: a run that does not start at k-slice 0 (its
-// partial goes to this cluster's slot); 2: a run from k-slice 0 that stops
-// short of K (finished with the partials of the later groups).
+// role 0: the whole K range; 1: a run that stops short of K (its fp32 partial
+// goes to this cluster's slot); 2: a run that ends at K but does not start at
+// k-slice 0 (finished with the partials of the earlier groups).
 struct WorkItem {
     int t, kb0, kb1, role;
 };
 
 struct SkCursor {
     int group, lane, round;
-    long long pos, end;
+    long long lo, hi;  // the group's split-block k-slices not yet walked: [lo, hi)
 };
 
 __device__ __forceinline__ long long sk_group_start(const GemmParams& p, int g) {
@@ -169,23 +169,30 @@ __device__ __forceinline__ void sk_begin(const GemmParams& p, int cluster, SkCur
     cur.round = 0;
     if (cur.group >= p.sk_groups) {  // spare cluster: no work
         cur.round = p.sk_rounds;
-        cur.pos = cur.end = 0;
+        cur.lo = cur.hi = 0;
         return;
     }
-    cur.pos = sk_group_start(p, cur.group);
-    cur.end = sk_group_start(p, cur.group + 1);
+    cur.lo = sk_group_start(p, cur.group);
+    cur.hi = sk_group_start(p, cur.group + 1);
 }
 
 // Next item of the cluster's static stream-K walk; false at the end. Every
-// role of a CTA walks the same sequence.
+// role of a CTA walks the same sequence. The split block is walked from the
+// group's last super-tile down to its first: the run that stops short of K
+// (a partial for a LATER group to finish) comes first, the run that finishes a
+// super-tile begun by EARLIER groups comes last. A finisher therefore only
+// ever waits for lower-numbered clusters; the hardware dispatches clusters in
+// index order, so whenever a finisher is resident its writers are resident or
+// done, even when other work holds some SMs.
 __device__ __forceinline__ bool sk_next(const GemmParams& p, SkCursor& cur, WorkItem& w) {
     const int nk = p.num_k_blocks;
-    if (cur.pos < cur.end) {
-        const long long tl = cur.pos / nk;
-        const int kb0 = static_cast<int>(cur.pos - tl * nk);
-        const int kb1 = static_cast<int>(min(static_cast<long long>(nk), kb0 + (cur.end - cur.pos)));
-        w = {static_cast<int>(tl), kb0, kb1, kb0 > 0 ? 1 : (kb1 < nk ? 2 : 0)};
-        cur.pos += kb1 - kb0;
+    if (cur.lo < cur.hi) {
+        const long long tl = (cur.hi - 1) / nk;
+        const long long lo = max(cur.lo, tl * nk);
+        const int kb0 = static_cast<int>(lo - tl * nk);
+        const int kb1 = static_cast<int>(cur.hi - tl * nk);
+        w = {static_cast<int>(tl), kb0, kb1, kb1 < nk ? 1 : (kb0 > 0 ? 2 : 0)};
+        cur.hi = lo;
         return true;
     }
     if (cur.round >= p.sk_rounds) return false;
@@ -547,13 +554,13 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
             if (sk) sk_tile_coords(t, cur.lane, p, mb, nb);
             else tile_coords(t, p, mb, nb);
             const int col0 = nb * kBN;
-            // A finisher (role 2) adds the partials of the later groups whose runs
-            // lie inside this super-tile, in k order: groups group+1 .. group+nwriters.
+            // A finisher (role 2) adds the partials of the earlier groups whose runs
+            // lie inside this super-tile, in k order: groups group-nwriters .. group-1.
             int nwriters = 0;
             if (role == 2) {
-                const long long tile_end = static_cast<long long>(t + 1) * p.num_k_blocks;
-                while (cur.group + 1 + nwriters < p.sk_groups &&
-                       sk_group_start(p, cur.group + 1 + nwriters) < tile_end) {
+                const long long tile_start = static_cast<long long>(t) * p.num_k_blocks;
+                while (cur.group - 1 - nwriters >= 0 &&
+                       sk_group_start(p, cur.group - nwriters) > tile_start) {
                     ++nwriters;
                 }
             }
@@ -569,7 +576,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 auto slot_of = [&](int cl) -> long long {
                     return ((static_cast<long long>(cl) * kCtaGroup + rank) * kSubM + sm) * kEpiWarps + q;
                 };
-                auto writer_cluster = [&](int w) { return (cur.group + 1 + w) * p.sk_lanes + cur.lane; };
+                auto writer_cluster = [&](int w) { return (cur.group - nwriters + w) * p.sk_lanes + cur.lane; };
                 auto partial_src = [&](int w) {
                     return reinterpret_cast<const float4*>(p.sk_partial) +
                            slot_of(writer_cluster(w)) * (32 * kBN / 4) + lane;
@@ -582,7 +589,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 const bool stage_in_tmem = p.sk_rounds == 0;
                 const uint32_t t_stage = tmem_base + (slot ^ 1) * kBN + (static_cast<uint32_t>(q * 32) << 16);
                 if (role == 2) {
-                    // Wait (bounded) for every later run's partial.
+                    // Wait (bounded) for every earlier run's partial.
                     bool got = true;
 #pragma unroll 1
                     for (int w = 0; w < nwriters && got; ++w) {
@@ -752,8 +759,8 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     }
                 };
                 if (role == 1) {
-                    // A run that does not start at k-slice 0: leave the fp32 partial in
-                    // this cluster's slot for the finisher; D is not written.
+                    // A run that stops short of K: leave the fp32 partial in this
+                    // cluster's slot for the finisher; D is not written.
                     float4* part = reinterpret_cast<float4*>(p.sk_partial) +
                                    slot_of(cluster) * (32 * kBN / 4) + lane;
                     int* flag = p.sk_flags + slot_of(cluster);
@@ -1052,6 +1059,32 @@ static int resolve_mode(int mode, int64_t m, int64_t n, int sm_count) {
     return B200_MODE_2CTA;
 }
 
+// Clusters (CTA pairs, or single CTAs in 1-CTA mode) of this kernel that fit
+// on the GPU at once: the persistent grid. Pairs use the occupancy query
+// (co-scheduling rules can leave fewer pairs than SMs / 2), falling back to
+// SMs / 2. Allocates nothing.
+static int resident_slots(const void* sym, int cta_group, int smem, int sm_count) {
+    if (cta_group == 1) return sm_count;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(sm_count, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    const cudaError_t err = cudaOccupancyMaxActiveClusters(&clusters, sym, &cfg);
+    if (err != cudaSuccess || clusters <= 0) {
+        cudaGetLastError();
+        clusters = sm_count / 2;
+    }
+    return std::max(clusters, 1);
+}
+
 static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
                        int64_t ldd, int out_dtype, int mode, void* stream, B200Plan** out_plan,
                        B200PlanInfo* out_info) {
@@ -1151,28 +1184,7 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
             delete plan;
             return cuda_fail("cudaFuncSetAttribute", err);
         }
-        if (plan->cta_group == 1) {
-            slots = props.sm_count;
-        } else {
-            cudaLaunchConfig_t cfg = {};
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = 2;
-            attr[0].val.clusterDim.y = 1;
-            attr[0].val.clusterDim.z = 1;
-            cfg.gridDim = dim3(props.sm_count, 1, 1);
-            cfg.blockDim = dim3(kThreads, 1, 1);
-            cfg.dynamicSmemBytes = plan->smem;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            int clusters = 0;
-            err = cudaOccupancyMaxActiveClusters(&clusters, sym, &cfg);
-            if (err != cudaSuccess || clusters <= 0) {
-                cudaGetLastError();
-                clusters = props.sm_count / 2;
-            }
-            slots = clusters;
-        }
+        slots = resident_slots(sym, plan->cta_group, plan->smem, props.sm_count);
         const int clusters = std::min(p.num_tiles, slots);
         plan->grid = clusters * plan->cta_group;
         if (stream_k_layout(p, slots, plan->sub_m)) {
@@ -1525,7 +1537,8 @@ int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, voi
 // ---------------------------------------------------------------------------
 // Allocation-free entry point.
 //
-// b200_gemm_noalloc runs the same kernel as b200_gemm, but the device scratch
+// b200_gemm_noalloc runs the same kernel as b200_gemm (always with the dynamic
+// tile schedule: stream-K's partial buffer does not fit), but the device scratch
 // the kernel needs -- its status word, where bounded waits record a timeout,
 // and the tile scheduler's counter -- lives in the file-scope array below
 // instead of a cudaMalloc'd buffer. Callers that cannot allocate device memory use it:
@@ -1538,27 +1551,46 @@ namespace b200 {
 constexpr size_t kNoAllocScratchBytes = 256;  // stated maximum of the static scratch
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch on `device`. In host code the array's
-// name is only a host-side stand-in, so the address is looked up once per
-// device with that device current and cached.
+// The current CUDA context (driver handle), or nullptr if it cannot be read.
+static void* current_context() {
+    using CtxGetCurrent = CUresult (*)(CUcontext*);
+    static CtxGetCurrent fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &ptr, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess || q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return static_cast<CtxGetCurrent>(nullptr);
+        }
+        return reinterpret_cast<CtxGetCurrent>(ptr);
+    }();
+    CUcontext ctx = nullptr;
+    if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+    return ctx;
+}
+
+// Device address of g_noalloc_scratch on `device` (the current device). In
+// host code the array's name is only a host-side stand-in, so the address is
+// looked up with the device current, checked, and cached per device together
+// with the context it belongs to: after a cudaDeviceReset the device gets a new
+// context (and the array a new address), so a changed context means a new lookup.
 static int noalloc_scratch_address(int device, void** out) {
     constexpr int kMaxDevices = 64;
     static void* addr[kMaxDevices] = {};
+    static void* ctx_of[kMaxDevices] = {};
     static std::mutex mu;
     if (device < 0 || device >= kMaxDevices) {
         set_error("device index %d out of range", device);
         return B200_ERR_INVALID_ARGUMENT;
     }
     std::lock_guard<std::mutex> lock(mu);
-    if (addr[device] == nullptr) {
-        int current = -1;
-        B200_CUDA_TRY(cudaGetDevice(&current));
-        if (current != device) B200_CUDA_TRY(cudaSetDevice(device));
+    void* ctx = current_context();
+    if (addr[device] == nullptr || ctx == nullptr || ctx != ctx_of[device]) {
         void* p = nullptr;
         const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (current != device) cudaSetDevice(current);
         if (err != cudaSuccess) return cuda_fail("cudaGetSymbolAddress(g_noalloc_scratch)", err);
         addr[device] = p;
+        ctx_of[device] = ctx;
     }
     *out = addr[device];
     return B200_OK;
@@ -1605,9 +1637,11 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
     plan->smem = smem_bytes_for(plan->cta_group, plan->sub_m);
     const void* sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, false);
     B200_CUDA_TRY(cudaFuncSetAttribute(sym, cudaFuncAttributeMaxDynamicSharedMemorySize, plan->smem));
-    // One CTA (pair) per SM (pair); the persistent kernel needs no more.
-    const int slots = plan->cta_group == 1 ? props.sm_count : props.sm_count / 2;
-    plan->grid = std::min(p.num_tiles, std::max(slots, 1)) * plan->cta_group;
+    if (plan->cta_group == 2)
+        B200_CUDA_TRY(cudaFuncSetAttribute(sym, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+    // The same persistent grid as plan_create's dynamic schedule.
+    const int slots = resident_slots(sym, plan->cta_group, plan->smem, props.sm_count);
+    plan->grid = std::min(p.num_tiles, slots) * plan->cta_group;
     return B200_OK;
 }
 

@@ -176,7 +176,7 @@ int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, voi
               int64_t ldd, int out_dtype, int mode, void* stream);
 
 /* Allocation-free GEMM. No counterpart in the reference. Same arguments,
- * kernel and synchronous behaviour as b200_gemm, but it calls no cudaMalloc,
+ * tile shapes, grid and synchronous behaviour as b200_gemm, but it calls no cudaMalloc,
  * cudaFree or other allocating routine: the kernel's only scratch (16 bytes:
  * the status word for bounded-wait timeouts and the tile scheduler's counter)
  * lives in a 256-byte static device
@@ -189,7 +189,13 @@ int b200_gemm(int64_t m, int64_t n, int64_t k, const void* a, const void* b, voi
  * share the array: each clears those 16 bytes before its launch, and calls
  * that overlap on the GPU (other streams, other threads) race on it. A launch
  * whose scratch need exceeded the array would be refused with
- * B200_ERR_UNSUPPORTED; this kernel needs 16 bytes whatever M, N and K are. */
+ * B200_ERR_UNSUPPORTED; this kernel needs 16 bytes whatever M, N and K are.
+ * It always runs the dynamic tile schedule: the stream-K schedule's partial
+ * buffer (about 19 MB) does not fit the static array, so on shapes where
+ * b200_gemm picks stream-K (e.g. 4096^3) the fp32 sums are associated
+ * differently and the last bits may differ (B200_GEMM_SCHEDULE is ignored).
+ * The cached address belongs to the device's current context; after a
+ * cudaDeviceReset the next call looks it up again. */
 int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
                       int64_t ldd, int out_dtype, int mode, void* stream);
 
@@ -371,6 +377,14 @@ int b200_shard_range(int64_t n, int64_t world, int64_t rank, int64_t granule, in
  * the bounded-wait machinery every kernel here relies on instead of the
  * reference's unbounded spins (src/memory/tma.cu:404-408). */
 int b200_selftest_bounded_wait(unsigned long long timeout_ns, int* status, void* stream);
+
+/* Launches `ctas` CTAs of 32 threads with smem_bytes of dynamic shared memory
+ * each (large enough to keep one CTA per SM) that hold their SMs for hold_ns
+ * (at most 5 s) of timer time and return. Stands in for another kernel sharing
+ * the GPU, so tests can check that a GEMM launched meanwhile on another stream
+ * completes correctly with only part of the SMs free. No counterpart in the
+ * reference. */
+int b200_selftest_occupy(int ctas, int smem_bytes, unsigned long long hold_ns, void* stream);
 
 #ifdef __cplusplus
 }

@@ -110,3 +110,65 @@ def test_invariants_over_random_shapes():
             assert p["sk_split_tiles"] * 3 >= p["sk_groups"]
             assert p["sk_rounds"] >= 1
             assert p["sk_groups"] * p["sk_lanes"] * cta == p["grid_ctas"]
+
+
+def _sk_walk(p):
+    """Restatement of the kernel's stream-K walk (sk_begin / sk_next in
+    csrc/gemm_sm100.cu): per group, the split-block items from its last
+    super-tile down to its first, then its whole-tile rounds."""
+    nk, groups = p["num_k_blocks"], p["sk_groups"]
+    iters = p["sk_split_tiles"] * nk
+    start = [g * iters // groups for g in range(groups + 1)]
+    walks = []
+    for g in range(groups):
+        lo, hi, items = start[g], start[g + 1], []
+        while lo < hi:
+            tl = (hi - 1) // nk
+            a = max(lo, tl * nk)
+            kb0, kb1 = a - tl * nk, hi - tl * nk
+            role = 1 if kb1 < nk else (2 if kb0 > 0 else 0)
+            items.append((tl, kb0, kb1, role))
+            hi = a
+        for r in range(p["sk_rounds"]):
+            items.append((p["sk_split_tiles"] + r * groups + g, 0, nk, 0))
+        walks.append(items)
+    return walks, start
+
+
+@pytest.mark.parametrize("shape,mode,sm", [
+    ((4096, 4096, 4096), "auto", 148), ((32768, 512, 4096), "auto", 148),
+    ((8192, 1792, 4096), "auto", 148), ((2304, 2304, 1024), "2cta", 148),
+    ((4096, 4096, 4096), "1cta", 148), ((5376, 2816, 4096), "auto", 132),
+    ((2560, 2560, 1000), "1cta", 16),
+])
+def test_stream_k_walk_covers_every_slice_and_waits_only_downward(monkeypatch, shape, mode, sm):
+    """Every k-slice of every super-tile is computed exactly once; a finisher only
+    waits for groups with a lower index (dispatched before it), so the schedule
+    completes even when not every cluster of the grid is resident."""
+    monkeypatch.setenv("B200_GEMM_SCHEDULE", "streamk")
+    p = pol(*shape, mode=mode, sm=sm)
+    assert p["schedule"] == "stream_k"
+    nk = p["num_k_blocks"]
+    walks, start = _sk_walk(p)
+    supers = p["sk_split_tiles"] + p["sk_rounds"] * p["sk_groups"]
+    seen = {}
+    for g, items in enumerate(walks):
+        split = [it for it in items if it[0] < p["sk_split_tiles"]]
+        writers = [i for i, it in enumerate(split) if it[3] == 1]
+        finishers = [i for i, it in enumerate(split) if it[3] == 2]
+        assert len(writers) <= 1 and len(finishers) <= 1
+        if writers:
+            assert writers[0] == 0  # the partial is produced first
+        if finishers:
+            assert finishers[0] == len(split) - 1  # the cut tile is finished last
+        for (t, kb0, kb1, role) in items:
+            for kb in range(kb0, kb1):
+                assert (t, kb) not in seen
+                seen[(t, kb)] = g
+            if role == 2:
+                tile_start = t * nk
+                deps = [w for w in range(g) if start[w + 1] > tile_start and start[w] < tile_start + nk]
+                assert deps and max(deps) < g
+                assert all(walks[w][0][0] == t and walks[w][0][3] == 1 for w in deps)
+    assert len(seen) == supers * nk
+    assert max(t for t, _ in seen) == supers - 1

@@ -192,3 +192,59 @@ def test_policy_preview_matches_plans(shape):
         assert pred["tile_m"] == info["tile_m"]
     finally:
         plan.destroy()
+
+
+_PARTIAL_RESIDENCY_CHILD = r"""
+import sys, time
+sys.path.insert(0, "gb300-gemm-anatomy_b200")
+import torch
+from b200gemm import _lib, gemm as G, operands
+torch.backends.cuda.matmul.allow_tf32 = False
+dev = torch.device("cuda", 0)
+lib = _lib.load()
+a, b = operands.integer_operands(4096, 4096, 4096, seed=31)
+a, b = a.to(dev), b.to(dev)
+ref = a.float() @ b.float().T
+sms = torch.cuda.get_device_properties(dev).multi_processor_count
+s_other, s_gemm = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+out = torch.full((4096, 4096), float("nan"), dtype=torch.float32, device=dev)
+plan = G.GemmPlan(a, b, out, mode="auto", stream=s_gemm)
+assert plan.schedule == "stream_k", plan.schedule
+for hold_ms in (1500, 0):
+    out.fill_(float("nan"))
+    torch.cuda.synchronize()
+    if hold_ms:
+        # Another tenant holds half of the SMs for longer than the wait limit.
+        rc = lib.b200_selftest_occupy(sms // 2, 200 * 1024, hold_ms * 1000000, s_other.cuda_stream)
+        assert rc == 0, _lib.last_error()
+        time.sleep(0.05)
+    t0 = time.perf_counter()
+    plan.execute()
+    plan.synchronize()
+    torch.cuda.synchronize()
+    print("ELAPSED", hold_ms, time.perf_counter() - t0)
+    print("MAXERR", hold_ms, float((out - ref).abs().max()))
+plan.destroy()
+"""
+
+
+def test_stream_k_completes_with_half_the_sms_taken():
+    """A stream-K launch that finds only part of its clusters resident still
+    finishes and is exact: finishers only wait for lower-numbered clusters.
+
+    Another kernel holds half the SMs for 1.5 s while the wait limit is 0.4 s,
+    so a finisher that waited for a cluster which cannot start yet would report
+    0x108 instead. Runs in a child process (the wait limit is read once per
+    process)."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    env = dict(os.environ, B200_WAIT_TIMEOUT_MS="400")
+    env.pop("B200_GEMM_SCHEDULE", None)
+    root = Path(__file__).resolve().parents[1]
+    res = subprocess.run([sys.executable, "-c", _PARTIAL_RESIDENCY_CHILD], cwd=root, env=env,
+                         capture_output=True, text=True, timeout=180)
+    assert res.returncode == 0, res.stderr[-3000:]
+    errs = [float(line.split()[2]) for line in res.stdout.splitlines() if line.startswith("MAXERR")]
+    assert errs == [0.0, 0.0], res.stdout
