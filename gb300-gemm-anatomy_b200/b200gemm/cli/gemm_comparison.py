@@ -22,6 +22,8 @@ import io
 import math
 import sys
 
+from . import row_contracts
+
 SCHEMA_VERSION = "b200.p35.1"
 EXPERIMENT = "gemm_comparison"
 UNIT = "b200_gemm"
@@ -58,17 +60,13 @@ CANDIDATES = (
 REF_BRIDGE = "baseline/_ref/libcublaslt_bridge_p35.so"
 BASELINE_VARIANTS = ("heuristic_first_supported", "torch_matmul")
 
-CSV_FIELDS = (
-    "schema_version", "experiment", "unit", "shape_index", "shape_id", "candidate_index",
-    "method", "variant", "m", "n", "k", "l", "ab_dtype", "acc_dtype", "c_dtype", "a_major",
-    "b_major", "c_major", "mma_tiler_m", "mma_tiler_n", "cluster_m", "cluster_n",
-    "use_2cta_instrs", "use_tma_store", "stages", "grid_ctas", "waves_count", "seed",
-    "operands", "reference", "atol", "rtol", "correctness", "max_abs_error", "max_rel_error",
-    "kernel_time_ms", "warmup_iterations", "iterations", "flop_count", "tflops",
-    "throughput_ratio_vs_cublaslt", "gap_to_cublaslt_pct", "rank_within_shape",
-    "roofline_fraction", "peak_tflops", "n_gpus", "gpu_name", "compute_capability",
-    "publishable",
-)
+# Rows carry the reference's 100 p35.v1 columns (src/gemm/gemm_comparison.py:324-440)
+# in its order; the default b200 schema appends the B200-specific columns.
+P35_FIELDS = row_contracts.P35_FIELDS
+B200_EXTRA_FIELDS = ("operands", "stages", "grid_ctas", "schedule", "roofline_fraction",
+                     "peak_tflops", "n_gpus")
+CSV_FIELDS = P35_FIELDS + B200_EXTRA_FIELDS
+KERNEL_SOURCE = "gb300-gemm-anatomy_b200/csrc/gemm_sm100.cu"
 
 
 class UsageError(Exception):
@@ -121,6 +119,10 @@ def build_arg_parser() -> argparse.ArgumentParser:
                         "heuristic_first_supported (the reference's cuBLASLt bridge)")
     p.add_argument("--schedule", choices=("auto", "dynamic", "streamk"), default="auto",
                    help="tile schedule of the B200 candidates (auto: the library's choice)")
+    p.add_argument("--schema", choices=("b200", "p35"), default="b200",
+                   help="p35: exactly the reference's 100 p35.v1 columns; b200: those plus "
+                        "the B200 columns (operands, stages, grid, schedule, roofline)")
+    p.add_argument("--run-kind", choices=("smoke", "benchmark"), default="smoke")
     p.add_argument("--peak-tflops", type=float, default=None,
                    help="roofline denominator (default: MEASURED_PEAKS.json bf16_tflops)")
     return p
@@ -158,12 +160,12 @@ def comparison_fields(flop: int, times_ms, variants):
     return out
 
 
-def format_csv(rows) -> str:
+def format_csv(rows, fields=CSV_FIELDS) -> str:
     buf = io.StringIO()
-    buf.write(",".join(CSV_FIELDS) + "\n")
+    buf.write(",".join(fields) + "\n")
     for r in rows:
         vals = []
-        for f in CSV_FIELDS:
+        for f in fields:
             v = r.get(f)
             if v is None:
                 vals.append("")
@@ -246,6 +248,27 @@ def _peak(args):
     return 1590.0
 
 
+def _ref_plan_info_type():
+    """ctypes mirror of the reference bridge's P35PlanInfo: 45 int64 members then three
+    doubles, in the order of src/gemm/cublaslt_bridge_p35.cu's struct (read back through
+    p35_plan_create's info argument; size checked against p35_plan_info_size)."""
+    import ctypes
+    ints = ("abi_version", "cublaslt_version", "shape_index", "m", "n", "k", "batch_count",
+            "lda", "ldb", "ldc", "ldd", "transa", "transb", "order_a", "order_b", "order_c",
+            "order_d", "type_a", "type_b", "type_c", "type_d", "compute_type", "scale_type",
+            "pointer_mode", "epilogue", "search_mode", "workspace_limit_bytes",
+            "workspace_bytes", "workspace_is_null", "heuristic_requested",
+            "heuristic_returned", "heuristic_index", "alignment_a_bytes", "alignment_b_bytes",
+            "alignment_c_bytes", "alignment_d_bytes", "algo_id", "tile_id", "stages_id",
+            "split_k", "reduction_scheme", "cta_swizzling", "custom_option", "inner_shape_id",
+            "cluster_shape_id")
+
+    class RefPlanInfo(ctypes.Structure):
+        _fields_ = [(n, ctypes.c_int64) for n in ints] + [
+            ("waves_count", ctypes.c_double), ("alpha", ctypes.c_double), ("beta", ctypes.c_double)]
+    return RefPlanInfo
+
+
 class _RefBridgePlan:
     """One plan of the reference's unmodified cuBLASLt bridge (p35_* C ABI)."""
 
@@ -264,14 +287,33 @@ class _RefBridgePlan:
         for name in ("p35_plan_execute", "p35_stream_synchronize", "p35_plan_destroy"):
             getattr(lib, name).restype = ctypes.c_int
             getattr(lib, name).argtypes = [ctypes.c_void_p]
-        self.info = ctypes.create_string_buffer(int(lib.p35_plan_info_size()))
+        info_t = _ref_plan_info_type()
+        if int(lib.p35_plan_info_size()) != ctypes.sizeof(info_t):
+            raise UsageError(f"reference bridge info size {int(lib.p35_plan_info_size())} != "
+                             f"mirror {ctypes.sizeof(info_t)}")
+        self.info = info_t()
         self.plan = ctypes.c_void_p()
         rc = lib.p35_plan_create(m, n, k, a.data_ptr(), b.data_ptr(), out.data_ptr(),
                                  out.data_ptr(), int(stream.cuda_stream), ctypes.byref(self.plan),
-                                 self.info)
+                                 ctypes.byref(self.info))
         if rc != 0:
             raise UsageError(f"reference bridge refused {m}x{n}x{k}: {lib.p35_last_error()!r}")
         self.lib = lib
+
+    def row_fields(self) -> dict:
+        """The cuBLASLt columns of a p35 row, as the reference writes them
+        (gemm_comparison.py:1578-1614)."""
+        i = self.info
+        out = dict(row_contracts.CUBLASLT_FROZEN_TEXT)
+        for f in ("lda", "ldb", "ldc", "ldd", "workspace_bytes", "alignment_a_bytes",
+                  "alignment_b_bytes", "alignment_c_bytes", "alignment_d_bytes",
+                  "heuristic_returned", "heuristic_index", "algo_id", "tile_id", "stages_id",
+                  "split_k", "reduction_scheme", "cta_swizzling", "custom_option",
+                  "inner_shape_id", "cluster_shape_id", "cublaslt_version"):
+            out[f] = int(getattr(i, f))
+        out["alpha"], out["beta"] = float(i.alpha), float(i.beta)
+        out["waves_count"] = float(i.waves_count)
+        return out
 
     def execute(self):
         if self.lib.p35_plan_execute(self.plan) != 0:
@@ -292,7 +334,43 @@ def ctypes_null():
     return ctypes.c_void_p()
 
 
+def _factory_sha256(opname: str) -> str:
+    """sha256 of the source that produced the operands (the reference records its
+    operand factory's source hash, gemm_comparison.py:3098-3125)."""
+    import hashlib
+    import inspect
+    from pathlib import Path
+    try:
+        if opname.startswith("cutlass"):
+            import cutlass.torch
+            src = inspect.getsourcefile(cutlass.torch)
+        else:
+            from .. import operands
+            src = inspect.getsourcefile(operands)
+        return hashlib.sha256(Path(src).read_bytes()).hexdigest()
+    except Exception:  # noqa: BLE001
+        return row_contracts.NOT_APPLICABLE
+
+
+def run_provenance(torch) -> dict:
+    """The provenance block of every row (gemm_comparison.py:1178-1230)."""
+    from pathlib import Path
+    dev = row_contracts.device_provenance(torch, 0)
+    kernel = Path(__file__).resolve().parents[3] / KERNEL_SOURCE
+    ident = row_contracts.file_identity(kernel) if kernel.is_file() else {"sha256": None, "blob": None}
+    return {"gpu_name": dev["gpu_name"], "gpu_uuid": dev["gpu_uuid"],
+            "compute_capability": dev["compute_capability"],
+            "driver_version": dev["driver_version"],
+            "cuda_toolkit_version": row_contracts.cuda_toolkit_version(),
+            "torch_cuda_version": dev["torch_cuda_version"],
+            "cutedsl_version": row_contracts.cutedsl_version(),
+            "kernel_sha256": ident["sha256"], "kernel_blob": ident["blob"],
+            **row_contracts.git_state()}
+
+
 def execute_measurement(args) -> str:
+    import time
+
     import torch
 
     from .. import check, operands
@@ -302,11 +380,11 @@ def execute_measurement(args) -> str:
         raise RuntimeError("no CUDA device is visible")
     torch.backends.cuda.matmul.allow_tf32 = False
     dev = torch.device("cuda", 0)
-    props = torch.cuda.get_device_properties(dev)
     shapes = args.shape if args.shape else SHAPE_SETS[args.shapes]
     cands = select_candidates(args.candidates)
     out_dtype = torch.float32 if args.out_dtype == "f32" else torch.bfloat16
     peak = _peak(args)
+    prov = run_provenance(torch)
     rows = []
     stream = torch.cuda.current_stream(dev)
     for si, (m, n, k) in enumerate(shapes):
@@ -331,16 +409,20 @@ def execute_measurement(args) -> str:
         for cand in cands:
             out.fill_(float("nan"))
             torch.cuda.synchronize()
+            t_setup = time.perf_counter()
+            extra = {}
             if cand["method"] == "b200":
                 plan = GemmPlan(a, b, out, mode=cand["mode"], stream=stream)
                 launch = plan.execute
                 meta = plan.info
+                extra["schedule"] = plan.schedule
             elif cand["method"] == "cublaslt":
                 if out_dtype != torch.float32:
                     raise UsageError("the reference cuBLASLt bridge writes fp32 D only")
                 plan = _RefBridgePlan(m, n, k, a, b, out, stream)
                 launch = plan.execute
                 meta = {}
+                extra.update(plan.row_fields())
             else:
                 plan = None
 
@@ -351,10 +433,16 @@ def execute_measurement(args) -> str:
                     else:
                         torch.mm(a, b.T, out_dtype=torch.float32, out=o)
                 meta = {}
+            setup_ms = (time.perf_counter() - t_setup) * 1e3 if plan is not None else None
+            f0 = torch.cuda.Event(enable_timing=True)
+            f1 = torch.cuda.Event(enable_timing=True)
+            f0.record(stream)
             launch()
+            f1.record(stream)
             if plan is not None:
                 plan.synchronize()
             torch.cuda.synchronize()
+            first_ms = f0.elapsed_time(f1)
             label = f"{m}x{n}x{k}/{cand['variant']}"
             if out_dtype == torch.float32:
                 max_abs, max_rel = check.validate_result(label, reference, out)
@@ -376,39 +464,64 @@ def execute_measurement(args) -> str:
                 plan.synchronize()
                 plan.destroy()
             times.append(e0.elapsed_time(e1) / args.iterations)
-            metas.append((cand, meta, max_abs, max_rel))
+            metas.append((cand, meta, max_abs, max_rel, setup_ms, first_ms, extra))
         flop = 2 * m * n * k
         comp = comparison_fields(flop, times, [c["variant"] for c in cands])
-        for ci, ((cand, meta, max_abs, max_rel), t, cf) in enumerate(zip(metas, times, comp)):
-            rows.append({
+        own = [i for i, c in enumerate(cands) if c["method"] == "b200"]
+        best_own = cands[min(own, key=lambda i: (times[i], i))]["variant"] if own else None
+        for ci, ((cand, meta, max_abs, max_rel, setup_ms, first_ms, extra), t, cf) in enumerate(
+                zip(metas, times, comp)):
+            own_kernel = cand["method"] == "b200"
+            cta = meta.get("cta_group") or 1
+            row = {
                 "schema_version": SCHEMA_VERSION, "experiment": EXPERIMENT, "unit": UNIT,
+                "run_kind": args.run_kind,
                 "shape_index": si, "shape_id": f"{m}x{n}x{k}x1", "candidate_index": ci,
                 "method": cand["method"], "variant": cand["variant"], "m": m, "n": n, "k": k,
                 "l": 1, "ab_dtype": "BFloat16", "acc_dtype": "Float32",
                 "c_dtype": "Float32" if out_dtype == torch.float32 else "BFloat16",
                 "a_major": "k", "b_major": "k", "c_major": "n",
-                "mma_tiler_m": cand["mma_tiler"][0] if cand["mma_tiler"] else None,
-                "mma_tiler_n": cand["mma_tiler"][1] if cand["mma_tiler"] else None,
-                "cluster_m": cand["cluster"][0] if cand["cluster"] else None,
-                "cluster_n": cand["cluster"][1] if cand["cluster"] else None,
-                "use_2cta_instrs": cand["use_2cta_instrs"],
-                "use_tma_store": cand["method"] == "b200",
-                "stages": meta.get("stages"), "grid_ctas": meta.get("grid_ctas"),
-                "waves_count": meta.get("waves"), "seed": seed, "operands": opname,
+                "seed": seed, "operands": opname,
                 "reference": "torch_fp32_ieee_einsum", "atol": check.REF_ATOL,
                 "rtol": check.REF_RTOL, "correctness": "PASS", "max_abs_error": max_abs,
-                "max_rel_error": max_rel, "kernel_time_ms": t,
+                "max_rel_error": max_rel, "setup_time_ms": setup_ms, "first_launch_ms": first_ms,
+                "kernel_time_ms": t, "cache_mode": "hot",
                 "warmup_iterations": args.warmup_iterations, "iterations": args.iterations,
-                "flop_count": flop, "roofline_fraction": cf["tflops"] / peak,
-                "peak_tflops": peak, "n_gpus": 1, "gpu_name": props.name,
-                "compute_capability": f"{props.major}.{props.minor}", "publishable": False,
-                **cf,
-            })
+                "flop_count": flop, "best_cutedsl_variant": best_own,
+                "is_best_cutedsl": cand["variant"] == best_own,
+                "roofline_fraction": cf["tflops"] / peak,
+                "peak_tflops": peak, "n_gpus": 1, "gpu_name": prov["gpu_name"],
+                "gpu_uuid": prov["gpu_uuid"], "compute_capability": prov["compute_capability"],
+                "driver_version": prov["driver_version"],
+                "cuda_toolkit_version": prov["cuda_toolkit_version"],
+                "torch_cuda_version": prov["torch_cuda_version"],
+                "cutedsl_version": prov["cutedsl_version"],
+                "operand_factory_sha256": _factory_sha256(opname),
+                "git_commit": prov["git_commit"], "git_dirty": prov["git_dirty"],
+                "publishable": False,
+                **cf, **extra,
+            }
+            if own_kernel:
+                row.update({
+                    "scheduler": f"{extra['schedule']}_persistent",
+                    "mma_tiler_m": meta.get("tile_m"), "mma_tiler_n": meta.get("tile_n"),
+                    "cluster_m": cta, "cluster_n": 1, "use_2cta_instrs": cta == 2,
+                    "use_tma_store": True,
+                    "max_active_clusters": (meta.get("grid_ctas") or 0) // cta,
+                    "upstream_kernel_file": KERNEL_SOURCE,
+                    "upstream_kernel_git_blob": prov["kernel_blob"],
+                    "upstream_kernel_sha256": prov["kernel_sha256"],
+                    "stages": meta.get("stages"), "grid_ctas": meta.get("grid_ctas"),
+                    "waves_count": meta.get("waves"),
+                })
+            rows.append(row)
             print(f"gemm_comparison: {m}x{n}x{k} {cand['variant']}: {t:.4f} ms "
                   f"{cf['tflops']:.1f} TFLOP/s max_abs={max_abs:.3g}", file=sys.stderr)
         del a, b, out, reference
         torch.cuda.empty_cache()
-    return format_csv(rows)
+    if args.schema == "p35":
+        return format_csv([row_contracts.p35_text(r) for r in rows], P35_FIELDS)
+    return format_csv([{**r, **row_contracts.p35_text(r)} for r in rows], CSV_FIELDS)
 
 
 def main(argv=None) -> int:

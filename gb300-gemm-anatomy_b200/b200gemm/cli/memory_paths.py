@@ -20,17 +20,15 @@ import time
 
 from .._lib import ERR_UNSUPPORTED, BridgeError
 
+from . import row_contracts
+
 SCHEMA_VERSION = "b200.mem.1"
-CSV_FIELDS = (
-    "schema_version", "timestamp_utc", "run_kind", "method", "sample_index", "stages",
-    "tile_width_bytes", "tile_height", "stage_bytes", "bytes_in_flight_per_sm", "vector_bytes",
-    "threads_per_cta", "target_ctas_per_sm", "occupancy_ctas_per_sm", "grid_blocks", "sm_count",
-    "smem_reservation_bytes", "l2_bytes", "requested_working_set_bytes", "working_set_bytes",
-    "working_set_l2_ratio", "passes", "useful_bytes", "warmup_ms", "kernel_time_ms",
-    "effective_gbps", "roofline_fraction", "hbm_peak_gbps", "correctness", "mismatches", "fill",
-    "checksum_xor", "checksum_sum", "host_checksum_xor", "host_checksum_sum", "gpu_name",
-    "compute_capability",
-)
+# The reference binaries' 37 columns (src/memory/ldgsts.cu:741-752, tma.cu:1028-1039)
+# in their order; the default b200 schema appends the roofline and checksum columns.
+REF_FIELDS = row_contracts.MEM_FIELDS
+B200_EXTRA_FIELDS = ("roofline_fraction", "hbm_peak_gbps", "fill", "checksum_xor", "checksum_sum",
+                     "host_checksum_xor", "host_checksum_sum")
+CSV_FIELDS = REF_FIELDS + B200_EXTRA_FIELDS
 
 
 def build_arg_parser():
@@ -49,6 +47,8 @@ def build_arg_parser():
     p.add_argument("--fill", choices=("pattern", "uniform"), default="pattern")
     p.add_argument("--sweep", choices=("reference", "baseline"))
     p.add_argument("--hbm-peak-gbps", type=float)
+    p.add_argument("--schema", choices=("b200", "ref"), default="b200",
+                   help="ref: exactly the reference binaries' 37 columns")
     return p
 
 
@@ -141,6 +141,7 @@ def run_one(buf, method, stages, stage_bytes, ctas, args, requested, peak, sampl
 
     dev = buf.device
     props = torch.cuda.get_device_properties(dev)
+    ident = _identity(dev.index or 0)
     nbytes = buf.numel() * buf.element_size()
     ws = (nbytes // stage_bytes) * stage_bytes
     view = buf.view(torch.uint8)[:ws]
@@ -179,7 +180,9 @@ def run_one(buf, method, stages, stage_bytes, ctas, args, requested, peak, sampl
                     "%Y-%m-%dT%H:%M:%SZ"),
                 "run_kind": args.run_kind or "self_test", "method": method,
                 "sample_index": sample_base + rep, "stages": stages,
+                "tile_width_elements": 64 if method == "tma_sw128" else 128,
                 "tile_width_bytes": 128 if method == "tma_sw128" else 256,
+                "copies_per_thread_per_stage": stage_bytes // (128 * 16),
                 "tile_height": stage_bytes // (128 if method == "tma_sw128" else 256),
                 "stage_bytes": stage_bytes, "bytes_in_flight_per_sm": stages * stage_bytes * ctas,
                 "vector_bytes": 16, "threads_per_cta": 128, "target_ctas_per_sm": ctas,
@@ -194,18 +197,36 @@ def run_one(buf, method, stages, stage_bytes, ctas, args, requested, peak, sampl
                 "checksum_xor": r["checksum_xor"] if args.fill == "uniform" else None,
                 "checksum_sum": r["checksum_sum"] if args.fill == "uniform" else None,
                 "host_checksum_xor": hx, "host_checksum_sum": hs, "gpu_name": props.name,
-                "compute_capability": f"{props.major}.{props.minor}",
+                "compute_capability": f"{props.major}.{props.minor}", **ident,
             })
     finally:
         plan.destroy()
     return rows
 
 
-def format_csv(rows):
-    out = [",".join(CSV_FIELDS)]
+_IDENTITY = {}
+
+
+def _identity(index):
+    """gpu_uuid, CUDA driver / runtime versions (cudaDriverGetVersion-style integers)
+    and this repository's git state: the reference row's provenance columns."""
+    if index not in _IDENTITY:
+        import torch
+
+        from .. import _lib
+        info = _lib.device_probe(index)
+        _IDENTITY[index] = {"gpu_uuid": f"GPU-{torch.cuda.get_device_properties(index).uuid}",
+                            "cuda_driver_version": info["driver_version"],
+                            "cuda_runtime_version": info["runtime_version"],
+                            **row_contracts.git_state()}
+    return _IDENTITY[index]
+
+
+def format_csv(rows, fields=CSV_FIELDS):
+    out = [",".join(fields)]
     for r in rows:
         out.append(",".join("" if r.get(f) is None else
-                            (f'"{r[f]}"' if "," in str(r[f]) else str(r[f])) for f in CSV_FIELDS))
+                            (f'"{r[f]}"' if "," in str(r[f]) else str(r[f])) for f in fields))
     return "\n".join(out) + "\n"
 
 
@@ -269,7 +290,7 @@ def main(argv=None) -> int:
     except Exception as exc:
         print(f"memory_paths: ERROR: {type(exc).__name__}: {exc}", file=sys.stderr)
         return 1
-    sys.stdout.write(format_csv(rows))
+    sys.stdout.write(format_csv(rows, REF_FIELDS if args.schema == "ref" else CSV_FIELDS))
     return 0
 
 

@@ -12,14 +12,19 @@ the benchmark config), --num-ctas (run the probe on every SM at once), and
 from __future__ import annotations
 
 import argparse
+import datetime
 import sys
 
-CSV_FIELDS = (
-    "schema_version", "method", "cta_group", "m", "n", "k", "depth", "iterations", "num_ctas",
-    "sample_index", "operands", "correctness", "leader_cycles", "flop_per_launch",
+from . import row_contracts
+
+# The reference binaries' 37 columns (src/compute/umma_1sm.cu:976-983, the same in
+# umma_2sm.cu) in their order; the default b200 schema appends the B200 columns.
+REF_FIELDS = row_contracts.UMMA_FIELDS
+B200_EXTRA_FIELDS = (
+    "schema_version_b200", "num_ctas", "operands", "leader_cycles", "flop_per_launch",
     "flops_per_cycle_per_sm", "kernel_time_ms", "tflops", "tflops_per_sm", "sm_count",
-    "gpu_name",
 )
+CSV_FIELDS = REF_FIELDS + B200_EXTRA_FIELDS
 
 
 def build_arg_parser():
@@ -34,7 +39,22 @@ def build_arg_parser():
     p.add_argument("--num-ctas", default="1", help="'1', 'all' (one CTA per SM) or a count")
     p.add_argument("--operands", choices=("pattern", "uniform"), default="pattern")
     p.add_argument("--sweep", action="store_true", help="all (mode, N, depth) combinations")
+    p.add_argument("--run-kind", choices=("smoke", "benchmark"), default="benchmark")
+    p.add_argument("--schema", choices=("b200", "ref"), default="b200",
+                   help="ref: exactly the reference binaries' 37 columns")
     return p
+
+
+def _identity():
+    """gpu_uuid, CUDA driver / runtime versions and git state (reference provenance)."""
+    import torch
+
+    from .. import _lib
+    info = _lib.device_probe(0)
+    return {"gpu_uuid": f"GPU-{torch.cuda.get_device_properties(0).uuid}",
+            "compute_capability": f"{info['cc_major']}.{info['cc_minor']}",
+            "cuda_driver_version": info["driver_version"],
+            "cuda_runtime_version": info["runtime_version"], **row_contracts.git_state()}
 
 
 def run_case(cta_group, n, depth, args, num_ctas, sms, name):
@@ -62,11 +82,12 @@ def run_case(cta_group, n, depth, args, num_ctas, sms, name):
         kc = np.arange(16)[:, None]
         B = ((2 * kc + c) % 5) - 2
         want = depth * (A @ B).astype(np.float64)
-        ok = np.array_equal(d.cpu().double().numpy(), want)
+        max_err = float(np.abs(d.cpu().double().numpy() - want).max())
+        ok = max_err == 0.0
     else:
         want = depth * (a.double() @ b.double().T).numpy()
-        ok = float(np.abs(d.cpu().double().numpy() - want).max()) <= \
-            depth * 16 * 2 ** -22 * (1 + np.abs(want).max())
+        max_err = float(np.abs(d.cpu().double().numpy() - want).max())
+        ok = max_err <= depth * 16 * 2 ** -22 * (1 + np.abs(want).max())
     if not ok:
         raise RuntimeError(f"UMMA {name} N={n} depth={depth}: D mismatch")
     rows = []
@@ -90,8 +111,21 @@ def run_case(cta_group, n, depth, args, num_ctas, sms, name):
         ms = e0.elapsed_time(e1)
         leader = int(cyc[0].item())
         total_flop = flop * ctas
+        total_umma = depth * args.iterations
         rows.append({
-            "schema_version": "b200.umma.1", "method": name, "cta_group": cta_group, "m": m,
+            "schema_version": "1", "schema_version_b200": "b200.umma.1",
+            "timestamp_utc": datetime.datetime.now(datetime.timezone.utc).strftime(
+                "%Y-%m-%dT%H:%M:%SZ"),
+            "run_kind": getattr(args, "run_kind", "benchmark"), "publishable": "false",
+            "warmup_iterations": args.warmup, "repetitions": args.repetitions,
+            "umma_per_iteration": depth, "total_umma": total_umma,
+            "flops_per_umma": 2 * m * n * 16, "total_flops": flop, "elapsed_cycles": leader,
+            "cycles_per_umma": f"{leader / total_umma:.6f}",
+            "flops_per_cycle": f"{flop / leader:.6f}" if leader else "0.000000",
+            "threads_per_cta": 128, "grid_blocks": ctas * cta_group, "tmem_columns": n,
+            "operand_path": "smem_smem", "input_type": "bf16", "accumulator_type": "fp32",
+            "mismatches": 0, "max_abs_error": f"{max_err:.6f}", **_identity(),
+            "method": name, "cta_group": cta_group, "m": m,
             "n": n, "k": 16, "depth": depth, "iterations": args.iterations, "num_ctas": ctas,
             "sample_index": rep, "operands": args.operands, "correctness": "OK",
             "leader_cycles": leader, "flop_per_launch": total_flop,
@@ -138,9 +172,10 @@ def main(argv=None) -> int:
     except Exception as exc:
         print(f"umma: ERROR: {type(exc).__name__}: {exc}", file=sys.stderr)
         return 1
-    out = [",".join(CSV_FIELDS)]
+    fields = REF_FIELDS if args.schema == "ref" else CSV_FIELDS
+    out = [",".join(fields)]
     for r in rows:
-        out.append(",".join(str(r[f]) for f in CSV_FIELDS))
+        out.append(",".join(f'"{r[f]}"' if "," in str(r[f]) else str(r[f]) for f in fields))
     sys.stdout.write("\n".join(out) + "\n")
     return 0
 

@@ -17,8 +17,12 @@ a CPU, imported from a checkout of the reference repository:
                      src/gemm/cublaslt_gemm.py:1568-1587) and for a small shape,
                      plus the small shape's fp32 einsum D (exact: integer operands).
   splitmix.json      SplitMix64 published value and the first pattern vectors.
+  row_contracts.json the reference's CSV headers: CSV_FIELDS of
+                     src/gemm/gemm_comparison.py (imported), and the header strings
+                     printed by print_csv_header in src/memory/ldgsts.cu, src/memory/tma.cu,
+                     src/compute/umma_1sm.cu and src/compute/umma_2sm.cu (read as text).
 
-Usage: python tests/golden/make_golden.py /path/to/reference
+Usage: python tests/golden/make_golden.py /path/to/reference [row_contracts]
 """
 from __future__ import annotations
 
@@ -41,6 +45,27 @@ from oracle import oracle  # noqa: E402
 
 def sha(t: torch.Tensor) -> str:
     return hashlib.sha256(t.contiguous().view(torch.int16).numpy().tobytes()).hexdigest()
+
+
+def _printed_header(source: Path) -> list:
+    """The column names printed by a reference binary's print_csv_header()."""
+    import re
+    text = source.read_text()
+    body = text[text.index("void print_csv_header()"):]
+    body = body[: body.index("}")]
+    literal = "".join(re.findall(r'"((?:[^"\\]|\\.)*)"', body))
+    return literal.replace("\\n", "").strip().split(",")
+
+
+def row_contracts(ref_root: Path) -> None:
+    sys.path.insert(0, str(ref_root / "src" / "gemm"))
+    import gemm_comparison as gc
+    out = {"p35": list(gc.CSV_FIELDS),
+           "memory": {n: _printed_header(ref_root / "src" / "memory" / f"{n}.cu")
+                      for n in ("ldgsts", "tma")},
+           "umma": {n: _printed_header(ref_root / "src" / "compute" / f"{n}.cu")
+                    for n in ("umma_1sm", "umma_2sm")}}
+    (HERE / "row_contracts.json").write_text(json.dumps(out, indent=1))
 
 
 def main(ref_root: Path) -> None:
@@ -125,10 +150,14 @@ def main(ref_root: Path) -> None:
         "seed0_first_output": oracle.SPLITMIX_SEED0_FIRST,
         "gamma": oracle.SPLITMIX_GAMMA,
         "pattern_words_0_64": words.tolist()}))
+    row_contracts(ref_root)
     print("golden fixtures written to", HERE)
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: python tests/golden/make_golden.py /path/to/reference")
-    main(Path(sys.argv[1]))
+    if len(sys.argv) not in (2, 3):
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/reference [row_contracts]")
+    if len(sys.argv) == 3 and sys.argv[2] == "row_contracts":
+        row_contracts(Path(sys.argv[1]))
+    else:
+        main(Path(sys.argv[1]))

@@ -98,3 +98,34 @@ def test_schedule_options_parse():
     r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--schedule", "sometimes"],
                        capture_output=True, text=True, timeout=120)
     assert r.returncode == 2 and "--schedule" in r.stderr
+
+
+def test_row_contracts_match_the_reference_headers():
+    """The drivers' reference schemas are the reference's own headers, column for
+    column (fixture extracted from its sources by tests/golden/make_golden.py)."""
+    import json
+    sys.path.insert(0, ENV_PATH)
+    from b200gemm.cli import gemm_comparison as gc, memory_paths as mp, row_contracts as rc, umma
+    g = json.loads((REPO / "tests" / "golden" / "row_contracts.json").read_text())
+    assert list(rc.P35_FIELDS) == g["p35"] and len(rc.P35_FIELDS) == 100
+    assert list(rc.MEM_FIELDS) == g["memory"]["ldgsts"] == g["memory"]["tma"]
+    assert list(rc.UMMA_FIELDS) == g["umma"]["umma_1sm"] == g["umma"]["umma_2sm"]
+    # The default b200 schemas keep the reference columns first, in order.
+    assert gc.CSV_FIELDS[:100] == rc.P35_FIELDS
+    assert mp.CSV_FIELDS[:37] == rc.MEM_FIELDS
+    assert umma.CSV_FIELDS[:37] == rc.UMMA_FIELDS
+    assert set(rc.KERNEL_ONLY_FIELDS) <= set(rc.P35_FIELDS)
+    assert set(rc.CUBLASLT_ONLY_FIELDS) <= set(rc.P35_FIELDS)
+
+
+def test_p35_value_conventions():
+    sys.path.insert(0, ENV_PATH)
+    from b200gemm.cli import row_contracts as rc
+    t = rc.p35_text({"kernel_time_ms": 0.5190001, "tflops": 2118.5, "max_abs_error": 0.0,
+                     "gap_to_cublaslt_pct": -12.5, "use_2cta_instrs": True, "m": 8192,
+                     "throughput_ratio_vs_cublaslt": 1.25, "atol": 0.1})
+    assert t["kernel_time_ms"] == "0.519000" and t["tflops"] == "2118.500000"
+    assert t["max_abs_error"] == "0.000000000" and t["gap_to_cublaslt_pct"] == "-12.500000"
+    assert t["use_2cta_instrs"] == "true" and t["m"] == "8192" and t["atol"] == "0.100000000"
+    assert t["throughput_ratio_vs_cublaslt"] == "1.250000000"
+    assert t["algo_id"] == "not_applicable" and len(t) == 100

@@ -86,3 +86,56 @@ def test_sharded_gemm_single_rank_gather():
     sg.destroy()
     ref = a.float() @ b.float().T
     assert float((full.cpu() - ref).abs().max()) <= 1e-3
+
+
+def _golden_headers():
+    import json
+    return json.loads((REPO / "tests" / "golden" / "row_contracts.json").read_text())
+
+
+def test_gemm_comparison_p35_schema_rows():
+    """--schema p35: exactly the reference's 100 columns, its value conventions
+    (not_applicable markers, fixed-point reals), the reference's own cuBLASLt bridge
+    row with its plan metadata when the bridge is built."""
+    cands = "persistent_auto,persistent_2cta,torch_matmul"
+    bridge = (REPO / "baseline" / "_ref" / "libcublaslt_bridge_p35.so").is_file()
+    if bridge:
+        cands += ",heuristic_first_supported"
+    r = run("b200gemm.cli.gemm_comparison", "--shape", "4096x4096x4096", "--schema", "p35",
+            "--iterations", "3", "--warmup-iterations", "1", "--candidates", cands)
+    assert r.returncode == 0, r.stderr
+    header = r.stdout.splitlines()[0].split(",")
+    assert header == _golden_headers()["p35"]
+    rows = list(csv.DictReader(io.StringIO(r.stdout)))
+    assert all(len(row) == 100 and "" not in row.values() for row in rows)
+    by = {row["variant"]: row for row in rows}
+    auto = by["persistent_auto"]
+    assert auto["scheduler"] == "stream_k_persistent" and auto["algo_id"] == "not_applicable"
+    assert auto["max_abs_error"] == "0.000000000" and auto["use_tma_store"] == "true"
+    assert int(auto["max_active_clusters"]) >= 1 and len(auto["upstream_kernel_sha256"]) == 64
+    assert by["persistent_2cta"]["best_cutedsl_variant"] in ("persistent_auto", "persistent_2cta")
+    assert by["torch_matmul"]["scheduler"] == "not_applicable"
+    assert auto["gpu_uuid"].startswith("GPU-")
+    if bridge:
+        lt = by["heuristic_first_supported"]
+        assert lt["order_a"] == "CUBLASLT_ORDER_ROW" and int(lt["algo_id"]) >= 0
+        assert lt["lda"] == "4096" and lt["scheduler"] == "not_applicable"
+
+
+def test_memory_and_umma_reference_schema_rows():
+    r = run("b200gemm.cli.memory_paths", "--method", "ldgsts", "--stages", "2",
+            "--stage-kib", "16", "--working-set-mib", "300", "--run-kind", "benchmark",
+            "--repetitions", "1", "--warmup-ms", "5", "--schema", "ref")
+    assert r.returncode == 0, r.stderr
+    g = _golden_headers()
+    assert r.stdout.splitlines()[0].split(",") == g["memory"]["ldgsts"]
+    row = next(csv.DictReader(io.StringIO(r.stdout)))
+    assert row["copies_per_thread_per_stage"] == "8" and row["gpu_uuid"].startswith("GPU-")
+    assert int(row["cuda_driver_version"]) > 0 and row["correctness"] == "OK"
+    r = run("b200gemm.cli.umma", "--mode", "2sm", "--n", "128", "--depth", "16",
+            "--iterations", "10", "--repetitions", "1", "--warmup", "1", "--schema", "ref")
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.splitlines()[0].split(",") == g["umma"]["umma_2sm"]
+    row = next(csv.DictReader(io.StringIO(r.stdout)))
+    assert row["method"] == "umma_2sm" and row["total_umma"] == "160"
+    assert row["flops_per_umma"] == str(2 * 256 * 128 * 16) and row["max_abs_error"] == "0.000000"
