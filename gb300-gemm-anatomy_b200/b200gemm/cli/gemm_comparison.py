@@ -52,6 +52,14 @@ CANDIDATES = (
      "cluster": None, "use_2cta_instrs": None},
     {"method": "cublas", "variant": "torch_matmul", "mode": None, "mma_tiler": None,
      "cluster": None, "use_2cta_instrs": None},
+    # NVIDIA's CuTe DSL Blackwell examples, the reference's three CuTe DSL candidates
+    # (gemm_comparison.py:214-265); context baselines, see cutedsl_baseline.py.
+    {"method": "cutedsl", "variant": "cutedsl_nonpersistent_1cta", "mode": None,
+     "mma_tiler": None, "cluster": None, "use_2cta_instrs": None},
+    {"method": "cutedsl", "variant": "cutedsl_persistent_1cta", "mode": None,
+     "mma_tiler": None, "cluster": None, "use_2cta_instrs": None},
+    {"method": "cutedsl", "variant": "cutedsl_persistent_2cta", "mode": None,
+     "mma_tiler": None, "cluster": None, "use_2cta_instrs": None},
     # The reference's own cuBLASLt bridge (cublaslt_bridge_p35.cu), built unmodified by
     # baseline/build_ref_bridge.sh; context baseline for its five frozen shapes, fp32 D.
     {"method": "cublaslt", "variant": "heuristic_first_supported", "mode": None,
@@ -116,7 +124,9 @@ def build_arg_parser() -> argparse.ArgumentParser:
                    help="comma list of persistent_auto, persistent_1cta, persistent_2cta, "
                         "persistent_2cta_m512, "
                         "torch_matmul, "
-                        "heuristic_first_supported (the reference's cuBLASLt bridge)")
+                        "heuristic_first_supported (the reference's cuBLASLt bridge), "
+                        "cutedsl_nonpersistent_1cta, cutedsl_persistent_1cta, "
+                        "cutedsl_persistent_2cta (NVIDIA's CuTe DSL examples)")
     p.add_argument("--schedule", choices=("auto", "dynamic", "streamk"), default="auto",
                    help="tile schedule of the B200 candidates (auto: the library's choice)")
     p.add_argument("--schema", choices=("b200", "p35"), default="b200",
@@ -423,6 +433,18 @@ def execute_measurement(args) -> str:
                 launch = plan.execute
                 meta = {}
                 extra.update(plan.row_fields())
+            elif cand["method"] == "cutedsl":
+                from . import cutedsl_baseline
+                ok, why = cutedsl_baseline.available()
+                if not ok:
+                    raise UsageError(f"{cand['variant']} is unavailable on this box: {why}")
+                plan = cutedsl_baseline.CuteDslPlan(cand["variant"], a, b, out, stream)
+                launch = plan.execute
+                meta = {}
+                ident = row_contracts.file_identity(plan.source)
+                extra.update(plan.meta)
+                extra.update({"upstream_kernel_git_blob": ident["blob"],
+                              "upstream_kernel_sha256": ident["sha256"]})
             else:
                 plan = None
 
@@ -433,7 +455,8 @@ def execute_measurement(args) -> str:
                     else:
                         torch.mm(a, b.T, out_dtype=torch.float32, out=o)
                 meta = {}
-            setup_ms = (time.perf_counter() - t_setup) * 1e3 if plan is not None else None
+            setup_ms = (time.perf_counter() - t_setup) * 1e3 \
+                if plan is not None and cand["method"] != "cutedsl" else None
             f0 = torch.cuda.Event(enable_timing=True)
             f1 = torch.cuda.Event(enable_timing=True)
             f0.record(stream)
@@ -467,7 +490,10 @@ def execute_measurement(args) -> str:
             metas.append((cand, meta, max_abs, max_rel, setup_ms, first_ms, extra))
         flop = 2 * m * n * k
         comp = comparison_fields(flop, times, [c["variant"] for c in cands])
-        own = [i for i, c in enumerate(cands) if c["method"] == "b200"]
+        # The best of the CuTe DSL rows when there are any (the reference's meaning),
+        # else the best of the B200 kernel's rows.
+        own = [i for i, c in enumerate(cands) if c["method"] == "cutedsl"] or \
+            [i for i, c in enumerate(cands) if c["method"] == "b200"]
         best_own = cands[min(own, key=lambda i: (times[i], i))]["variant"] if own else None
         for ci, ((cand, meta, max_abs, max_rel, setup_ms, first_ms, extra), t, cf) in enumerate(
                 zip(metas, times, comp)):

@@ -139,3 +139,25 @@ def test_memory_and_umma_reference_schema_rows():
     row = next(csv.DictReader(io.StringIO(r.stdout)))
     assert row["method"] == "umma_2sm" and row["total_umma"] == "160"
     assert row["flops_per_umma"] == str(2 * 256 * 128 * 16) and row["max_abs_error"] == "0.000000"
+
+
+def test_gemm_comparison_cutedsl_context_rows():
+    """NVIDIA's CuTe DSL examples as context candidates beside ours (fp32 D,
+    integer operands: every candidate exact)."""
+    sys.path.insert(0, str(REPO / "gb300-gemm-anatomy_b200"))
+    from b200gemm.cli import cutedsl_baseline
+    ok, why = cutedsl_baseline.available()
+    if not ok:
+        pytest.skip(why)
+    r = run("b200gemm.cli.gemm_comparison", "--shape", "1024x512x256", "--iterations", "2",
+            "--warmup-iterations", "1", "--candidates",
+            "persistent_auto,cutedsl_nonpersistent_1cta,cutedsl_persistent_1cta,"
+            "cutedsl_persistent_2cta", timeout=900)
+    assert r.returncode == 0, r.stderr[-3000:]
+    rows = list(csv.DictReader(io.StringIO(r.stdout)))
+    assert [row["method"] for row in rows] == ["b200", "cutedsl", "cutedsl", "cutedsl"]
+    for row in rows:
+        assert float(row["max_abs_error"]) == 0.0
+    assert rows[3]["use_2cta_instrs"] == "true" and rows[3]["mma_tiler_m"] == "256"
+    assert float(rows[2]["compile_time_ms"]) > 0 and rows[1]["max_active_clusters"] == "not_applicable"
+    assert rows[0]["best_cutedsl_variant"].startswith("cutedsl_")
