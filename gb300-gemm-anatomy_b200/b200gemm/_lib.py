@@ -143,6 +143,7 @@ SIGNATURES = {
     "b200_peer_buffer_free": (_INT, [_P]),
     "b200_peer_open": (_INT, [_P, ctypes.POINTER(_P)]),
     "b200_peer_close": (_INT, [_P]),
+    "b200_peer_copy_2d": (_INT, [_P, _I64, _P, _I64, _I64, _I64, _P]),
     "b200_gemm_noalloc": (_INT, [_I64, _I64, _I64, _P, _P, _P, _I64, _INT, _INT, _P]),
     "b200_fill_pattern": (_INT, [_P, _I64, _P]),
     "b200_stream_plan_create": (_INT, [ctypes.POINTER(StreamConfig), _P, _I64, _INT,

@@ -2,13 +2,15 @@
 
 Run one process per GPU (torchrun --nproc-per-node G ... -m b200gemm.cli.dist_gemm).
 Config: M=8192 activations ~ N(0,1), weights ~ N(0,0.02), seed 2 (the LLM
-projection config); every rank draws the same global B from the seed and keeps
-its shard. For each shape it checks the gathered D against a torch fp32
+projection config), drawn on the device; every rank draws the same global B
+from the seed and keeps its shard. For each shape it checks the gathered D against a torch fp32
 reference on sampled rows, then times (CUDA events, max over ranks):
   none   the sharded GEMM alone (weak scaling of the compute)
   nccl   GEMM, then NCCL all-gather of the bf16 shards and the re-layout
   p2p    the fused gather: the GEMM epilogue TMA-stores every tile to every peer
   p2p_st the fused gather with per-thread 16-byte stores instead of TMA
+  ce     GEMM, then the copy engines copy this rank's columns into every peer's
+         full buffer (no SM work, no re-layout)
 Prints one CSV row per (shape, gather) on rank 0.
 """
 from __future__ import annotations
@@ -26,7 +28,7 @@ def main(argv=None) -> int:
     ap.add_argument("--shape", action="append", help="NxK (repeatable); default: the LLM shapes")
     ap.add_argument("--iterations", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--gathers", default="none,nccl,p2p,p2p_st")
+    ap.add_argument("--gathers", default="none,nccl,p2p,p2p_st,ce")
     args = ap.parse_args(argv)
     import torch
     import torch.distributed as dist
@@ -42,24 +44,26 @@ def main(argv=None) -> int:
     shapes = [tuple(int(x) for x in s.split("x")) for s in args.shape] if args.shape else SHAPES
     rows = []
     for (n, k) in shapes:
-        a_h, b_h = operands.llm_operands(n, k, m=args.m)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        a, b_full = operands.llm_operands_device(n, k, dev, m=args.m)
         n0, n1 = bdist.shard_bounds(n, world, rank)
-        a = a_h.to(dev)
-        b = b_h[n0:n1].contiguous().to(dev)
-        idx = torch.arange(0, args.m, max(args.m // 64, 1))
-        ref = a_h[idx].float() @ b_h.float().T
+        b = b_full[n0:n1].contiguous()
+        idx = torch.arange(0, args.m, max(args.m // 64, 1), device=dev)
+        ref = (a[idx].float() @ b_full.float().T).cpu()
+        del b_full
         for gather in args.gathers.split(","):
             # p2p: fused gather with TMA bulk stores to the peers; p2p_st: 16-byte stores.
             if gather == "p2p_st":
                 os.environ["B200_PEER_STORES"] = "st"
             else:
                 os.environ.pop("B200_PEER_STORES", None)
-            sg = bdist.ShardedGemm(a, b, n, p2p=gather.startswith("p2p"))
+            sg = bdist.ShardedGemm(a, b, n, p2p=gather.startswith("p2p") or gather == "ce",
+                                   engine="ce" if gather == "ce" else "sm")
             mode = "none" if gather == "none" else "full"
             full = sg.run(mode)
             torch.cuda.synchronize()
             if gather != "none":
-                got = full[idx.to(dev)].float().cpu()
+                got = full[idx].float().cpu()
                 rel = float((got - ref).norm() / ref.norm())
                 if rel > 1e-2:
                     raise RuntimeError(f"{n}x{k} {gather}: rel err {rel}")

@@ -160,9 +160,11 @@ def device_provenance(torch, index: int = 0) -> dict:
         pynvml.nvmlShutdown()
     except Exception:  # noqa: BLE001 - NVML absent: the field says so
         driver = None
-    rt = torch.cuda.cudart().cudaRuntimeGetVersion() if hasattr(torch.cuda, "cudart") else None
-    if isinstance(rt, tuple):
-        rt = rt[-1]
+    try:
+        from .. import _lib
+        rt = _lib.device_probe(index)["runtime_version"]
+    except Exception:  # noqa: BLE001
+        rt = None
     return {"gpu_name": props.name, "gpu_uuid": f"GPU-{props.uuid}",
             "compute_capability": f"{props.major}.{props.minor}",
             "driver_version": driver or "not_available",

@@ -11,10 +11,14 @@ only when the caller asks for it:
   gather="blocks"  NCCL all-gather of the padded shards into [world, M, W]
   gather="full"    the same, then one re-layout to row-major M x N
   p2p=True         fused gather: the GEMM's epilogue writes every output chunk
-                   into every rank's row-major M x N buffer over NVLink (plain
-                   16-byte stores through CUDA IPC mappings), so the exchange
-                   overlaps the math tile by tile and needs no re-layout; one
-                   NCCL all-reduce of a scalar then orders the ranks.
+                   into every rank's row-major M x N buffer over NVLink (TMA
+                   bulk stores, or 16-byte stores, through CUDA IPC mappings),
+                   so the exchange overlaps the math tile by tile and needs no
+                   re-layout; one NCCL all-reduce of a scalar then orders the ranks.
+  p2p=True, engine="ce"
+                   the same buffers, but the GEMM writes only its own columns
+                   and the copy engines then copy them into every peer's buffer
+                   (one 2D copy per peer, each on its own stream), SMs idle.
 
 One process per GPU; the process group is torch.distributed over NCCL (or
 gloo for CPU tests of the host logic, with `local_gemm` injected).
@@ -90,7 +94,8 @@ class ShardedGemm:
     """D = A @ B^T with B (and D) split by output columns across the group."""
 
     def __init__(self, a: torch.Tensor, b_shard: torch.Tensor, n_total: int, *, group=None,
-                 out_dtype=torch.bfloat16, mode: str = "auto", local_gemm=None, p2p: bool = False):
+                 out_dtype=torch.bfloat16, mode: str = "auto", local_gemm=None, p2p: bool = False,
+                 engine: str = "sm"):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -104,6 +109,9 @@ class ShardedGemm:
         self.a, self.b = a, b_shard
         self._plan = None
         self.p2p = p2p
+        if engine not in ("sm", "ce"):
+            raise ValueError("engine must be 'sm' (fused epilogue stores) or 'ce' (copy engines)")
+        self.engine = engine
         self.peer_buffer = None
         if p2p:
             if local_gemm is not None or out_dtype != torch.bfloat16:
@@ -121,7 +129,7 @@ class ShardedGemm:
             from .gemm import GemmPlan
             if self.n1 > self.n0 and self.m > 0:
                 self._plan = GemmPlan(a, b_shard, self.out, mode=mode)
-                if p2p:
+                if p2p and engine == "sm":
                     pitch_off = self.n0 * 2
                     self._plan.set_peers([self.peer_buffer.peers[r] + pitch_off
                                           for r in sorted(self.peer_buffer.peers)])
@@ -134,9 +142,30 @@ class ShardedGemm:
     def launches_per_step(self) -> int:
         return self._plan.launches_per_execute if self._plan is not None else 0
 
+    def _copy_to_peers(self):
+        """Copy-engine gather: this rank's columns into every peer's full buffer."""
+        lib = self.peer_buffer._lib
+        cur = torch.cuda.current_stream(self.a.device)
+        if not hasattr(self, "_ce_streams"):
+            self._ce_streams = [torch.cuda.Stream(self.a.device) for _ in self.peer_buffer.peers]
+        done = torch.cuda.Event()
+        done.record(cur)
+        pitch = self.n_total * 2
+        src = self.out.data_ptr()
+        for s, r in zip(self._ce_streams, sorted(self.peer_buffer.peers)):
+            s.wait_event(done)
+            _lib.check(lib.b200_peer_copy_2d(self.peer_buffer.peers[r] + self.n0 * 2, pitch, src, pitch,
+                                             (self.n1 - self.n0) * 2, self.m, s.cuda_stream),
+                       "b200_peer_copy_2d", lib)
+            ev = torch.cuda.Event()
+            ev.record(s)
+            cur.wait_event(ev)
+
     def run(self, gather: str = "none"):
         self._local()
         if self.p2p:
+            if self.engine == "ce" and self.world > 1 and self.n1 > self.n0:
+                self._copy_to_peers()
             # Order the ranks: after this all-reduce every rank's kernel (and its
             # peer writes, fenced system-wide before exit) has completed.
             if self._flag is None:

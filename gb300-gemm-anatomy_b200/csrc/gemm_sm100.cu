@@ -129,6 +129,14 @@ struct GemmParams {
     // partial writers skip their flag, so finishers' bounded waits run out and
     // report B200_DEV_TIMEOUT_PARTIAL. Nothing faults or hangs.
     int sk_test_drop_flags;
+    // L2 eviction priorities of the operand loads: 0 none; 1 the operand the
+    // raster group reuses (A for m-groups, B for n-groups) evict_last and the
+    // streamed one evict_first.
+    int l2_hint;
+    // K walk direction: 1 = tiles of odd waves (tile id / kserp_wave) run
+    // their k-slices from the last to the first, so a wave starts on the
+    // k-slices the previous wave left most recently in L2.
+    int kserp_wave;
 };
 
 // Tensor maps of the peers' D slices for the TMA form of the fused gather.
@@ -328,6 +336,9 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         if (elect_one()) {
             uint32_t stage = 0, phase = 0, qs = 0, qph = 0;
             long long issued = 0;  // ring slots armed so far (failure-path drain)
+            const uint64_t keep = l2_policy_evict_last(), stream_pol = l2_policy_evict_first();
+            const uint64_t pol_a = p.raster_n ? stream_pol : keep;
+            const uint64_t pol_b = p.raster_n ? keep : stream_pol;
             bool ok = true;
             // The leader fetches the first tile id now and each later one while the
             // current tile is still loading (see fetch_kb).
@@ -383,8 +394,10 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 // trip, late enough that a fast pair cannot take two tiles while a
                 // slow one has none.
                 const int fetch_kb = max(0, p.num_k_blocks - 2 * kStages);
-                for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!sk && rank == 0 && kb == fetch_kb) next = atomicAdd(&p.tile_counter[0], 1);
+                const bool rev = !sk && p.kserp_wave > 0 && ((t / p.kserp_wave) & 1);
+                for (int i = kb0; i < kb1; ++i) {
+                    const int kb = rev ? kb0 + kb1 - 1 - i : i;
+                    if (!sk && rank == 0 && i == fetch_kb) next = atomicAdd(&p.tile_counter[0], 1);
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.status, p.timeout_ns,
                                    B200_DEV_TIMEOUT_PRODUCER)) {
                         ok = false;
@@ -395,13 +408,23 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     const uint32_t fb = full0 + 8 * stage;
                     if constexpr (!kPair) {
                         mbar_arrive_expect_tx(fb, C::kStageBytes);
-                        tma_load_2d(sa, &tmA, fb, kb * kBK, a_row);
-                        tma_load_2d(sb, &tmB, fb, kb * kBK, b_row);
+                        if (p.l2_hint) {
+                            tma_load_2d_hint(sa, &tmA, fb, kb * kBK, a_row, pol_a);
+                            tma_load_2d_hint(sb, &tmB, fb, kb * kBK, b_row, pol_b);
+                        } else {
+                            tma_load_2d(sa, &tmA, fb, kb * kBK, a_row);
+                            tma_load_2d(sb, &tmB, fb, kb * kBK, b_row);
+                        }
                     } else {
                         const uint32_t leader_fb = mapa_shared(fb, 0);
                         if (rank == 0) mbar_arrive_expect_tx(fb, 2 * C::kStageBytes);
-                        tma_load_2d_pair(sa, &tmA, leader_fb, kb * kBK, a_row);
-                        tma_load_2d_pair(sb, &tmB, leader_fb, kb * kBK, b_row);
+                        if (p.l2_hint) {
+                            tma_load_2d_pair_hint(sa, &tmA, leader_fb, kb * kBK, a_row, pol_a);
+                            tma_load_2d_pair_hint(sb, &tmB, leader_fb, kb * kBK, b_row, pol_b);
+                        } else {
+                            tma_load_2d_pair(sa, &tmA, leader_fb, kb * kBK, a_row);
+                            tma_load_2d_pair(sb, &tmB, leader_fb, kb * kBK, b_row);
+                        }
                     }
                     ++issued;
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -1187,6 +1210,8 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
         slots = resident_slots(sym, plan->cta_group, plan->smem, props.sm_count);
         const int clusters = std::min(p.num_tiles, slots);
         plan->grid = clusters * plan->cta_group;
+        if (const char* e = std::getenv("B200_GEMM_L2HINT")) p.l2_hint = e[0] == '1';
+        if (const char* e = std::getenv("B200_GEMM_KSERP")) p.kserp_wave = e[0] == '1' ? clusters : 0;
         if (stream_k_layout(p, slots, plan->sub_m)) {
             plan->grid = p.sk_groups * p.sk_lanes * plan->cta_group;
             const void* sk_sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, true);

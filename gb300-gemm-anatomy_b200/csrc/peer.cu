@@ -66,4 +66,23 @@ int b200_peer_close(void* ptr) {
     B200_ABI_GUARD_END
 }
 
+int b200_peer_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                      int64_t width_bytes, int64_t rows, void* stream) {
+    B200_ABI_GUARD_BEGIN
+    b200::clear_error();
+    if (dst == nullptr || src == nullptr || width_bytes < 0 || rows < 0 || dst_pitch < width_bytes ||
+        src_pitch < width_bytes) {
+        b200::set_error("peer_copy_2d: non-NULL pointers and pitches >= width required");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (width_bytes == 0 || rows == 0) return B200_OK;
+    // A device-to-device 2D copy: with `dst` in another GPU's memory (an IPC
+    // mapping) the copy engines move it over NVLink, with no SM involved.
+    B200_CUDA_TRY(cudaMemcpy2DAsync(dst, static_cast<size_t>(dst_pitch), src, static_cast<size_t>(src_pitch),
+                                    static_cast<size_t>(width_bytes), static_cast<size_t>(rows),
+                                    cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+    return B200_OK;
+    B200_ABI_GUARD_END
+}
+
 }  // extern "C"

@@ -200,8 +200,10 @@ int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a, const void
                       int64_t ldd, int out_dtype, int mode, void* stream);
 
 /* Fused gather for the N-sharded multi-GPU GEMM. After set_peers, every launch
- * also writes each output chunk into the npeers (<= 7) peer buffers with
- * 16-byte stores over NVLink, at the same rows/columns and row pitch as the
+ * also writes each staged output chunk into the npeers (<= 7) peer buffers over
+ * NVLink -- by default as TMA bulk stores (one per peer per chunk, through
+ * tensor maps encoded here), with B200_PEER_STORES=st at set_peers as per-thread
+ * 16-byte stores -- at the same rows/columns and row pitch as the
  * plan's own D; peer_d[g] must already point at this shard's first column in
  * peer g's full matrix (see b200_peer_*). The caller orders the ranks after
  * the launch (e.g. one NCCL all-reduce of a scalar) before reading peers'
@@ -217,6 +219,13 @@ int b200_peer_buffer_alloc(int64_t bytes, void** out_ptr, void* out_handle);
 int b200_peer_buffer_free(void* ptr);
 int b200_peer_open(const void* handle, void** out_ptr);
 int b200_peer_close(void* ptr);
+/* Copy-engine gather step: an asynchronous 2D device copy of `rows` rows of
+ * width_bytes from src (row pitch src_pitch bytes) to dst (pitch dst_pitch) on
+ * `stream`; dst may be a peer buffer opened with b200_peer_open, so the copy
+ * engines carry this shard to that GPU over NVLink while the SMs stay free. No
+ * counterpart in the reference (no multi-GPU path there). */
+int b200_peer_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                      int64_t width_bytes, int64_t rows, void* stream);
 
 /* Timeline tracing (off by default). trace: device buffer of grid_ctas x 64
  * uint64 (%globaltimer ns) that each later execute fills per CTA: [0] entry,
