@@ -21,7 +21,7 @@ alone as the reference arm.
 Further sections of the same JSON line (after the headline's timed region;
 `--no-extras` skips them):
   llm_shard    (every N) config c5, 8192 x {128256, 14336} x 4096, N split over
-               the ranks (strong scaling), gathers none / fused / nccl, each
+               the ranks (strong scaling), gathers none / fused / fused_mc / nccl, each
                checked on every rank against torch IEEE fp32 on 64 sampled rows
                before it is timed (max over ranks)
   sustained    (N=1) >= 2 s windows of back-to-back 8192^3 launches, ours and
@@ -321,7 +321,8 @@ def llm_shard_section(world, rank, dev, shapes=((128256, 4096), (14336, 4096)), 
     """Config c5 N-sharded over the ranks (strong scaling: N fixed, split by
     b200_shard_range), each gather timed: none (the shard GEMM alone), fused
     (the GEMM epilogue stores every output chunk into every rank's full D over
-    NVLink) and nccl (GEMM, then NCCL all-gather + re-layout). Before timing,
+    NVLink), fused_mc (the same through an NVLink multicast address: one store,
+    replicated by the switch) and nccl (GEMM, then NCCL all-gather + re-layout). Before timing,
     every rank checks the full gathered D (its own shard with gather none) on
     64 sampled rows against torch's IEEE fp32 matmul with the bf16 rule;
     the results are combined over ranks."""
@@ -331,7 +332,7 @@ def llm_shard_section(world, rank, dev, shapes=((128256, 4096), (14336, 4096)), 
     from b200gemm import check, dist as bdist, operands
 
     torch.backends.cuda.matmul.allow_tf32 = False
-    gathers = ("none", "fused", "nccl") if world > 1 else ("none",)
+    gathers = ("none", "fused", "fused_mc", "nccl") if world > 1 else ("none",)
     out = {"operands": "c5: A ~ N(0,1), B ~ N(0,0.02), seed 2, drawn on the device",
            "scaling": "strong: N fixed, split over the ranks", "check_rows": 64, "shapes": {}}
     for (n, k) in shapes:
@@ -344,7 +345,12 @@ def llm_shard_section(world, rank, dev, shapes=((128256, 4096), (14336, 4096)), 
         del b_full
         res = {"shard_cols": n1 - n0}
         for gather in gathers:
-            sg = bdist.ShardedGemm(a, b, n, p2p=(gather == "fused"))
+            try:
+                sg = bdist.ShardedGemm(a, b, n, p2p=gather.startswith("fused"),
+                                       engine="mc" if gather == "fused_mc" else "sm")
+            except RuntimeError as exc:  # e.g. no NVLink multicast on this node
+                res[gather] = {"unavailable": str(exc)}
+                continue
             mode = "none" if gather == "none" else "full"
             got = sg.run(mode)
             torch.cuda.synchronize()

@@ -138,6 +138,7 @@ SIGNATURES = {
     "b200_gemm_policy": (_INT, [_I64, _I64, _I64, _INT, _INT, ctypes.POINTER(PolicyInfo)]),
     "b200_gemm_plan_set_trace": (_INT, [_P, _P, _I64]),
     "b200_gemm_plan_set_peers": (_INT, [_P, _INT, ctypes.POINTER(_P)]),
+    "b200_gemm_plan_set_multicast": (_INT, [_P, _P]),
     "b200_ipc_handle_size": (ctypes.c_size_t, []),
     "b200_peer_buffer_alloc": (_INT, [_I64, ctypes.POINTER(_P), _P]),
     "b200_peer_buffer_free": (_INT, [_P]),

@@ -11,6 +11,8 @@ reference on sampled rows, then times (CUDA events, max over ranks):
   p2p_st the fused gather with per-thread 16-byte stores instead of TMA
   ce     GEMM, then the copy engines copy this rank's columns into every peer's
          full buffer (no SM work, no re-layout)
+  mc     the fused gather through NVLink multicast: each output chunk is written
+         once to a multicast address and the switch replicates it to every GPU
 Prints one CSV row per (shape, gather) on rank 0.
 """
 from __future__ import annotations
@@ -28,7 +30,7 @@ def main(argv=None) -> int:
     ap.add_argument("--shape", action="append", help="NxK (repeatable); default: the LLM shapes")
     ap.add_argument("--iterations", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--gathers", default="none,nccl,p2p,p2p_st,ce")
+    ap.add_argument("--gathers", default="none,nccl,p2p,mc,ce")
     args = ap.parse_args(argv)
     import torch
     import torch.distributed as dist
@@ -57,8 +59,8 @@ def main(argv=None) -> int:
                 os.environ["B200_PEER_STORES"] = "st"
             else:
                 os.environ.pop("B200_PEER_STORES", None)
-            sg = bdist.ShardedGemm(a, b, n, p2p=gather.startswith("p2p") or gather == "ce",
-                                   engine="ce" if gather == "ce" else "sm")
+            sg = bdist.ShardedGemm(a, b, n, p2p=gather.startswith("p2p") or gather in ("ce", "mc"),
+                                   engine=gather if gather in ("ce", "mc") else "sm")
             mode = "none" if gather == "none" else "full"
             full = sg.run(mode)
             torch.cuda.synchronize()

@@ -15,6 +15,12 @@ only when the caller asks for it:
                    bulk stores, or 16-byte stores, through CUDA IPC mappings),
                    so the exchange overlaps the math tile by tile and needs no
                    re-layout; one NCCL all-reduce of a scalar then orders the ranks.
+  p2p=True, engine="mc"
+                   the multicast form of the fused gather: the full buffer is
+                   torch symmetric memory bound to an NVLink multicast object,
+                   and the epilogue writes each output chunk ONCE to the
+                   multicast address; the NVSwitch replicates it into every
+                   rank's buffer (each GPU sends its shard once, not once per peer).
   p2p=True, engine="ce"
                    the same buffers, but the GEMM writes only its own columns
                    and the copy engines then copy them into every peer's buffer
@@ -90,6 +96,27 @@ class PeerBuffer:
             self.ptr = 0
 
 
+class MulticastBuffer:
+    """This rank's full-matrix output in torch symmetric memory, bound with every
+    other rank's to one NVLink multicast object (multicast_ptr)."""
+
+    def __init__(self, m: int, n: int, device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        grp = group if group is not None else dist.group.WORLD
+        self.tensor = symm_mem.empty((m, n), dtype=torch.bfloat16, device=device)
+        self._handle = symm_mem.rendezvous(self.tensor, grp)
+        self.mc_ptr = int(self._handle.multicast_ptr)
+        if self.mc_ptr == 0:
+            raise RuntimeError("this GPU group has no NVLink multicast (NVLS) support")
+        if self.mc_ptr % 16 != 0:
+            raise RuntimeError("multicast mapping is not 16-byte aligned")
+        self.peers = {}
+
+    def close(self):
+        self._handle = None
+        self.tensor = None
+
+
 class ShardedGemm:
     """D = A @ B^T with B (and D) split by output columns across the group."""
 
@@ -109,8 +136,9 @@ class ShardedGemm:
         self.a, self.b = a, b_shard
         self._plan = None
         self.p2p = p2p
-        if engine not in ("sm", "ce"):
-            raise ValueError("engine must be 'sm' (fused epilogue stores) or 'ce' (copy engines)")
+        if engine not in ("sm", "ce", "mc"):
+            raise ValueError("engine must be 'sm' (fused epilogue stores), 'mc' (fused multicast "
+                             "stores) or 'ce' (copy engines)")
         self.engine = engine
         self.peer_buffer = None
         if p2p:
@@ -118,7 +146,10 @@ class ShardedGemm:
                 raise ValueError("the fused gather runs the B200 kernel with bf16 output")
             if self.n_total % 8 != 0:
                 raise ValueError("the fused gather needs N % 8 == 0 (16-byte rows)")
-            self.peer_buffer = PeerBuffer(self.m, self.n_total, group)
+            if engine == "mc":
+                self.peer_buffer = MulticastBuffer(self.m, self.n_total, a.device, group)
+            else:
+                self.peer_buffer = PeerBuffer(self.m, self.n_total, group)
             self.full = self.peer_buffer.tensor
             self.out = self.full[:, self.n0:self.n1]
         else:
@@ -129,6 +160,8 @@ class ShardedGemm:
             from .gemm import GemmPlan
             if self.n1 > self.n0 and self.m > 0:
                 self._plan = GemmPlan(a, b_shard, self.out, mode=mode)
+                if p2p and engine == "mc":
+                    self._plan.set_multicast(self.peer_buffer.mc_ptr + self.n0 * 2)
                 if p2p and engine == "sm":
                     pitch_off = self.n0 * 2
                     self._plan.set_peers([self.peer_buffer.peers[r] + pitch_off

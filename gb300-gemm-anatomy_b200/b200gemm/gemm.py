@@ -92,6 +92,12 @@ class GemmPlan:
         _lib.check(self._lib.b200_gemm_plan_set_peers(self._plan, len(peer_ptrs), arr),
                    "b200_gemm_plan_set_peers", self._lib)
 
+    def set_multicast(self, mc_ptr: int) -> None:
+        """Multicast gather: also write every output chunk once to this NVLink
+        multicast address (this shard's first column of the full D); 0 = off."""
+        _lib.check(self._lib.b200_gemm_plan_set_multicast(self._plan, ctypes.c_void_p(int(mc_ptr) or None)),
+                   "b200_gemm_plan_set_multicast", self._lib)
+
     TRACE_SLOTS = 64
 
     def enable_trace(self) -> torch.Tensor:

@@ -101,6 +101,11 @@ struct GemmParams {
     int peer_tma;    // 1: peer chunks go out as TMA bulk stores (PeerMaps), 0: 16-byte stores
     long long ldd;
     void* peer_d[kMaxPeers];
+    // Multicast gather (NVLS): every staged chunk is also written once, with
+    // 16-byte multimem stores, at the same row/column of this multicast
+    // address (already at this shard's first column, row pitch ldd); the switch
+    // replicates it into every GPU's full D. nullptr: off.
+    void* mc_d;
     // Stream-K schedule (sk_iters > 0; otherwise the dynamic schedule above).
     // The clusters form sk_groups groups of sk_lanes; group g, lane l is
     // cluster g * sk_lanes + l (clusters past the last group get no work). A
@@ -751,6 +756,21 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         }
                         bulk_commit_group();
                     }
+                    if (p.mc_d != nullptr) {
+                        // Multicast gather: 8 lanes cover one 128-byte staged row, one
+                        // 16-byte multimem store each; the switch fans it out to all GPUs.
+                        constexpr int kElem = 128 / kColsPerChunk;
+                        const int piece = lane & 7;
+                        const int pcol = col + piece * (16 / kElem);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int r = (lane >> 3) + 4 * i;
+                            if (row0 + r >= p.m || pcol >= p.n) continue;
+                            const uint4 v = ld_shared_v4(sbuf + r * 128 + ((piece ^ (r & 7)) << 4));
+                            const long long off = (static_cast<long long>(row0 + r) * p.ldd + pcol) * kElem;
+                            multimem_st_v4(static_cast<uint8_t*>(p.mc_d) + off, v);
+                        }
+                    }
                     if (p.npeers > 0 && !p.peer_tma) {
                         // Fused gather: 8 lanes cover one 128-byte staged row, so each
                         // warp store writes four contiguous 128-byte row segments.
@@ -861,7 +881,7 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
             }
         }
         if (lane == 0) bulk_wait_group<0>();
-        if (p.npeers > 0) __threadfence_system();  // peer writes visible before exit
+        if (p.npeers > 0 || p.mc_d != nullptr) __threadfence_system();  // peer writes visible before exit
         __syncwarp();
         if (warp == 2 && lane == 0) trace_stamp(p, 4);
     }
@@ -1445,6 +1465,21 @@ int b200_gemm_plan_set_peers(B200Plan* plan, int npeers, void* const* peer_d) {
     plan->params.peer_tma = use_tma;
     plan->params.ldd = plan->info.ldd;
     for (int g = 0; g < b200::kMaxPeers; ++g) plan->params.peer_d[g] = g < npeers ? peer_d[g] : nullptr;
+    return B200_OK;
+}
+
+int b200_gemm_plan_set_multicast(B200Plan* plan, void* mc_d) {
+    b200::clear_error();
+    if (plan == nullptr || reinterpret_cast<uintptr_t>(mc_d) % 16 != 0) {
+        b200::set_error("set_multicast: plan must be valid and mc_d 16-byte aligned (or NULL)");
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (mc_d != nullptr && (plan->out_f32 || (plan->info.ldd * 2) % 16 != 0)) {
+        b200::set_error("set_multicast: the multicast gather needs bf16 D with 16-byte rows");
+        return B200_ERR_UNSUPPORTED;
+    }
+    plan->params.mc_d = mc_d;
+    plan->params.ldd = plan->info.ldd;
     return B200_OK;
 }
 

@@ -485,6 +485,15 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* addr) {
     return v;
 }
 
+// 16-byte store to an NVLink multicast address (NVLS): the switch writes the
+// same bytes into every GPU bound to the multicast object. Bit-preserving (no
+// arithmetic); weak ordering, fenced by the caller.
+__device__ __forceinline__ void multimem_st_v4(void* mc_addr, uint4 v) {
+    asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};"
+                 ::"l"(mc_addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
 __device__ __forceinline__ void st_release_gpu(int* addr, int v) {
     asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }

@@ -211,6 +211,18 @@ int b200_gemm_noalloc(int64_t m, int64_t n, int64_t k, const void* a, const void
  * multi-GPU path there); replaces GEMM-then-all-gather with one kernel. */
 int b200_gemm_plan_set_peers(B200Plan* plan, int npeers, void* const* peer_d);
 
+/* Multicast form of the fused gather (NVLink SHARP / NVLS). mc_d is this
+ * shard's first column inside an NVLink multicast mapping of the full M x N
+ * bf16 output that every rank has bound its own buffer to (for example
+ * torch.distributed._symmetric_memory's multicast_ptr plus n0 * 2); row pitch
+ * = the plan's ldd. Every launch then writes each output chunk once, with
+ * 16-byte multimem stores, and the switch replicates it into every GPU's
+ * buffer: each GPU sends its shard once instead of once per peer. The caller
+ * orders the ranks after the launch, as for set_peers. NULL turns it off.
+ * Plain stores only: no TMA or bulk load ever reads a multicast or peer
+ * address. No counterpart in the reference (no multi-GPU path there). */
+int b200_gemm_plan_set_multicast(B200Plan* plan, void* mc_d);
+
 /* Peer-visible buffers (CUDA IPC) for the fused gather. alloc: cudaMalloc of
  * `bytes` plus its IPC handle (b200_ipc_handle_size() bytes written to
  * out_handle); open/close map another process's buffer on the current device. */

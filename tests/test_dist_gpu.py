@@ -1,9 +1,11 @@
 """N-sharded GEMM on every visible GPU (skipped with fewer than 2).
 
 Each rank runs the B200 kernel on its output columns; the full matrix is
-gathered either with one NCCL all-gather or by the kernel itself (fused
-gather: peer stores over NVLink), and compared on every rank with the CPU
-oracle. NVLS is off (NCCL_NVLS_ENABLE=0) and no multicast object is used.
+gathered with one NCCL all-gather, by the kernel itself (fused gather: peer
+stores over NVLink, or multicast stores through an NVLS object where the node
+has one), or by the copy engines, and compared on every rank with the CPU
+oracle. NCCL's own NVLS is off (NCCL_NVLS_ENABLE=0); every rank stays up for
+the whole test (no rank leaves while its memory is bound to a multicast object).
 """
 import os
 import socket
@@ -55,6 +57,25 @@ def _worker(rank, world, port, q):
                     torch.cuda.synchronize()
                     check.bf16_tolerance_check(f"rank {rank} p2p={p2p} {mode}", ref, full.cpu(), k,
                                                1.0, 1.0)
+                sg.destroy()
+        # The multicast form of the fused gather (NVLS), where the node has it;
+        # copy-engine gather always.
+        os.environ.pop("B200_PEER_STORES", None)
+        for engine in ("mc", "ce"):
+            for mode in ("2cta", "2cta_m512", "1cta"):
+                try:
+                    sg = bdist.ShardedGemm(a.to(dev), b[n0:n1].contiguous().to(dev), n, mode=mode,
+                                           p2p=True, engine=engine)
+                except RuntimeError as exc:
+                    if engine == "mc" and "multicast" in str(exc):
+                        break  # no NVLS on this node: nothing to check for this engine
+                    raise
+                for _ in range(2):
+                    full = sg.run("full")
+                    sg.synchronize()
+                    torch.cuda.synchronize()
+                    check.bf16_tolerance_check(f"rank {rank} engine={engine} {mode}", ref, full.cpu(),
+                                               k, 1.0, 1.0)
                 sg.destroy()
         # Stream-K per shard (forced): cut tiles are finished by the epilogue that
         # also sends the output chunks to the peers.
