@@ -92,7 +92,7 @@ PolicyInfo = _i64_struct(
     "B200PolicyInfo",
     ["mode", "tile_m", "tile_n", "num_m_blocks", "num_n_blocks", "num_k_blocks", "num_tiles",
      "clusters", "raster_n", "group", "schedule", "sk_groups", "sk_lanes", "sk_lane_n",
-     "sk_rounds", "sk_split_tiles", "grid_ctas"],
+     "sk_rounds", "sk_split_tiles", "grid_ctas", "kserp_wave"],
     doubles=["waves"],
 )
 

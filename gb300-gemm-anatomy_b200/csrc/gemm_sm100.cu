@@ -134,13 +134,12 @@ struct GemmParams {
     // partial writers skip their flag, so finishers' bounded waits run out and
     // report B200_DEV_TIMEOUT_PARTIAL. Nothing faults or hangs.
     int sk_test_drop_flags;
-    // L2 eviction priorities of the operand loads: 0 none; 1 the operand the
-    // raster group reuses (A for m-groups, B for n-groups) evict_last and the
-    // streamed one evict_first.
-    int l2_hint;
-    // K walk direction: 1 = tiles of odd waves (tile id / kserp_wave) run
-    // their k-slices from the last to the first, so a wave starts on the
-    // k-slices the previous wave left most recently in L2.
+    // K walk direction of the dynamic schedule ("K serpentine"): with
+    // kserp_wave > 0, the tiles of odd waves (tile id / kserp_wave odd) run
+    // their k-slices from the last to the first, so each wave starts on the
+    // k-slices the previous wave left most recently in L2 instead of on the
+    // ones it evicted first. The direction is a function of the tile id alone,
+    // so results stay bit-identical from launch to launch.
     int kserp_wave;
 };
 
@@ -341,9 +340,6 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         if (elect_one()) {
             uint32_t stage = 0, phase = 0, qs = 0, qph = 0;
             long long issued = 0;  // ring slots armed so far (failure-path drain)
-            const uint64_t keep = l2_policy_evict_last(), stream_pol = l2_policy_evict_first();
-            const uint64_t pol_a = p.raster_n ? stream_pol : keep;
-            const uint64_t pol_b = p.raster_n ? keep : stream_pol;
             bool ok = true;
             // The leader fetches the first tile id now and each later one while the
             // current tile is still loading (see fetch_kb).
@@ -413,23 +409,13 @@ gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     const uint32_t fb = full0 + 8 * stage;
                     if constexpr (!kPair) {
                         mbar_arrive_expect_tx(fb, C::kStageBytes);
-                        if (p.l2_hint) {
-                            tma_load_2d_hint(sa, &tmA, fb, kb * kBK, a_row, pol_a);
-                            tma_load_2d_hint(sb, &tmB, fb, kb * kBK, b_row, pol_b);
-                        } else {
-                            tma_load_2d(sa, &tmA, fb, kb * kBK, a_row);
-                            tma_load_2d(sb, &tmB, fb, kb * kBK, b_row);
-                        }
+                        tma_load_2d(sa, &tmA, fb, kb * kBK, a_row);
+                        tma_load_2d(sb, &tmB, fb, kb * kBK, b_row);
                     } else {
                         const uint32_t leader_fb = mapa_shared(fb, 0);
                         if (rank == 0) mbar_arrive_expect_tx(fb, 2 * C::kStageBytes);
-                        if (p.l2_hint) {
-                            tma_load_2d_pair_hint(sa, &tmA, leader_fb, kb * kBK, a_row, pol_a);
-                            tma_load_2d_pair_hint(sb, &tmB, leader_fb, kb * kBK, b_row, pol_b);
-                        } else {
-                            tma_load_2d_pair(sa, &tmA, leader_fb, kb * kBK, a_row);
-                            tma_load_2d_pair(sb, &tmB, leader_fb, kb * kBK, b_row);
-                        }
+                        tma_load_2d_pair(sa, &tmA, leader_fb, kb * kBK, a_row);
+                        tma_load_2d_pair(sb, &tmB, leader_fb, kb * kBK, b_row);
                     }
                     ++issued;
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -1079,6 +1065,17 @@ static void raster_for(const GemmParams& p, int tile_m, int sub_m, int* group, i
     if (const char* r = std::getenv("B200_GEMM_RASTER")) *raster_n = (r[0] == 'n' || r[0] == 'N');
 }
 
+// K serpentine for the dynamic schedule: on unless B200_GEMM_KSERP=0.
+// Measured on B200 (ncu, 8192^3 512 x 256 tiles): DRAM reads 818 -> 661 MB per
+// launch and 673 -> 667 us; an L2 evict_last / evict_first policy on the
+// operand loads was tried beside it and read more (878 MB) and ran slower.
+static int kserp_wave_for(int clusters) {
+    if (const char* e = std::getenv("B200_GEMM_KSERP")) {
+        if (e[0] == '0') return 0;
+    }
+    return clusters;
+}
+
 // AUTO: small problems that cannot fill the pairs run 1-CTA tiles. Otherwise
 // the pair-tile shape with the better score wins, score = waves / ceil(waves)
 // (the fraction of the last wave that is busy) x 1.03 for 512 x 256 tiles,
@@ -1230,8 +1227,7 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
         slots = resident_slots(sym, plan->cta_group, plan->smem, props.sm_count);
         const int clusters = std::min(p.num_tiles, slots);
         plan->grid = clusters * plan->cta_group;
-        if (const char* e = std::getenv("B200_GEMM_L2HINT")) p.l2_hint = e[0] == '1';
-        if (const char* e = std::getenv("B200_GEMM_KSERP")) p.kserp_wave = e[0] == '1' ? clusters : 0;
+        p.kserp_wave = kserp_wave_for(clusters);
         if (stream_k_layout(p, slots, plan->sub_m)) {
             plan->grid = p.sk_groups * p.sk_lanes * plan->cta_group;
             const void* sk_sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, true);
@@ -1557,6 +1553,7 @@ int b200_gemm_policy(int64_t m, int64_t n, int64_t k, int mode, int sm_count, B2
     o.sk_rounds = p.sk_rounds;
     o.sk_split_tiles = sk ? p.sk_iters / p.num_k_blocks : 0;
     o.grid_ctas = grid;
+    o.kserp_wave = sk ? 0 : b200::kserp_wave_for(clusters);
     o.waves = static_cast<double>(p.num_tiles) / slots;
     return B200_OK;
     B200_ABI_GUARD_END
@@ -1702,6 +1699,7 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
     // The same persistent grid as plan_create's dynamic schedule.
     const int slots = resident_slots(sym, plan->cta_group, plan->smem, props.sm_count);
     plan->grid = std::min(p.num_tiles, slots) * plan->cta_group;
+    p.kserp_wave = kserp_wave_for(plan->grid / plan->cta_group);
     return B200_OK;
 }
 

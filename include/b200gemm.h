@@ -288,6 +288,8 @@ typedef struct B200PolicyInfo {
     int64_t sk_rounds;       /* whole-tile rounds after the split block */
     int64_t sk_split_tiles;  /* super-tiles in the split block */
     int64_t grid_ctas;
+    int64_t kserp_wave;      /* dynamic schedule: tiles of odd waves of this many tiles walk K
+                                backwards (0 = off, and always 0 under stream-K) */
     double waves;            /* num_tiles / clusters */
 } B200PolicyInfo;
 
