@@ -114,10 +114,10 @@ class ClockSampler:
                                      nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0))
             except Exception:  # noqa: BLE001
                 break
-            stop.wait(0.005)
+            stop.wait(0.001)
 
     def start(self):
-        # NVML read every 5 ms (read-only queries); nvidia-smi as the fallback
+        # NVML read every 1 ms (read-only queries); nvidia-smi as the fallback
         # (or when B200_BENCH_CLOCKS=smi).
         got = None if os.environ.get("B200_BENCH_CLOCKS") == "smi" else self._nvml_handle()
         if got is not None:
@@ -180,10 +180,15 @@ class ClockSampler:
                 "sw_thermal_slowdown": nvml.nvmlClocksEventReasonSwThermalSlowdown,
                 "sw_power_cap": nvml.nvmlClocksEventReasonSwPowerCap}
         lo, hi = getattr(self, "t_start", None), getattr(self, "t_end", None)
+        samples = self.samples
+        if lo is not None and hi is not None:
+            inside = [x for x in samples if lo <= x[0] <= hi]
+            if not inside and samples:
+                # A timed region shorter than the polling gap: the sample closest to it.
+                inside = [min(samples, key=lambda x: min(abs(x[0] - lo), abs(x[0] - hi)))]
+            samples = inside
         sm, mx, reasons = [], [], set()
-        for ts, clk, clk_max, mask, _ in self.samples:
-            if lo is not None and hi is not None and not (lo <= ts <= hi):
-                continue
+        for ts, clk, clk_max, mask, _ in samples:
             sm.append(float(clk))
             mx.append(float(clk_max))
             reasons.update(name for name, bit in bits.items() if mask & bit)
@@ -193,7 +198,7 @@ class ClockSampler:
             pass
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm), "source": "nvml, 5 ms"}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvml, 1 ms"}
 
     def stop(self):
         if getattr(self, "nvml", None) is not None:

@@ -31,6 +31,7 @@ MODE_AUTO = 0
 MODE_1CTA = 1
 MODE_2CTA = 2
 MODE_2CTA_M512 = 3
+MODE_2CTA_N128 = 4
 
 STREAM_LDGSTS = 0
 STREAM_TMA = 1

@@ -47,6 +47,8 @@ CANDIDATES = (
      "cluster": (2, 1), "use_2cta_instrs": True},
     {"method": "b200", "variant": "persistent_2cta_m512", "mode": "2cta_m512",
      "mma_tiler": (512, 256), "cluster": (2, 1), "use_2cta_instrs": True},
+    {"method": "b200", "variant": "persistent_2cta_n128", "mode": "2cta_n128",
+     "mma_tiler": (256, 128), "cluster": (2, 1), "use_2cta_instrs": True},
     # The library's own choice per shape (B200_MODE_AUTO).
     {"method": "b200", "variant": "persistent_auto", "mode": "auto", "mma_tiler": None,
      "cluster": None, "use_2cta_instrs": None},
@@ -122,7 +124,7 @@ def build_arg_parser() -> argparse.ArgumentParser:
     p.add_argument("--out-dtype", choices=("f32", "bf16"), default="f32")
     p.add_argument("--candidates", default="persistent_auto,torch_matmul",
                    help="comma list of persistent_auto, persistent_1cta, persistent_2cta, "
-                        "persistent_2cta_m512, "
+                        "persistent_2cta_m512, persistent_2cta_n128, "
                         "torch_matmul, "
                         "heuristic_first_supported (the reference's cuBLASLt bridge), "
                         "cutedsl_nonpersistent_1cta, cutedsl_persistent_1cta, "

@@ -21,7 +21,7 @@ from ._lib import BridgeError
 
 _DTYPE_CODE = {torch.bfloat16: _lib.OUT_BF16, torch.float32: _lib.OUT_F32}
 _MODE_CODE = {"auto": _lib.MODE_AUTO, "1cta": _lib.MODE_1CTA, "2cta": _lib.MODE_2CTA,
-              "2cta_m512": _lib.MODE_2CTA_M512}
+              "2cta_m512": _lib.MODE_2CTA_M512, "2cta_n128": _lib.MODE_2CTA_N128}
 
 
 def _stream_handle(stream) -> int:

@@ -44,7 +44,7 @@
 namespace b200 {
 
 constexpr int kBK = 64;            // K elements per ring slot (128 bytes: one swizzle atom row)
-constexpr int kBN = 256;           // MMA N: columns of D per tile
+constexpr int kBN = 256;           // MMA N: columns of D per tile (the 2CTA_N128 tile: 128)
 constexpr int kRowsPerCta = 128;   // D rows per CTA per tile (TMEM lanes)
 constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
@@ -59,13 +59,17 @@ constexpr int kMaxPeers = 7;            // fused gather: up to 8 GPUs           
 // slots hold the tile's two row halves; each is handed back to the MMA warp as
 // soon as the epilogue has drained it. Per k-slice a CTA then loads 48 KiB for
 // 2 x 4.2 MFLOP instead of 32 KiB for 4.2 MFLOP: 25 % fewer L2->SM bytes.
-template <int kCtaGroup, int kSubM>
+// kTileN = 128 (pair mode, one accumulator per tile): 256 x 128 pair tiles,
+// twice as many tiles as 256 x 256, for shapes whose 256-wide tiles leave the
+// last wave half empty; the smaller stages give the ring eight slots.
+template <int kCtaGroup, int kSubM, int kTileN = kBN>
 struct GemmCfg {
     static_assert(kSubM == 1 || (kSubM == 2 && kCtaGroup == 2), "unsupported tile shape");
-    static constexpr int kStages = (kCtaGroup == 1 || kSubM == 2) ? 4 : 6;
+    static_assert(kTileN == kBN || (kTileN == 128 && kCtaGroup == 2 && kSubM == 1), "unsupported tile N");
+    static constexpr int kStages = kTileN == 128 ? 8 : ((kCtaGroup == 1 || kSubM == 2) ? 4 : 6);
     static constexpr int kARows = kRowsPerCta * kSubM;
     static constexpr int kABytes = kARows * kBK * 2;
-    static constexpr int kBRows = kBN / kCtaGroup;
+    static constexpr int kBRows = kTileN / kCtaGroup;
     static constexpr int kBBytes = kBRows * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kTileM = kARows * kCtaGroup;
@@ -244,12 +248,16 @@ __device__ __forceinline__ void sk_tile_coords(int t, int lane, const GemmParams
 
 // kStreamK selects the stream-K schedule at compile time, so the dynamic
 // schedule's kernels carry none of its code (it measured 0.4-1 % on them).
-template <int kCtaGroup, int kSubM, bool kOutF32, bool kStreamK>
+template <int kCtaGroup, int kSubM, bool kOutF32, bool kStreamK, int kTileN = kBN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tn_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmD, const GemmParams p,
                      const __grid_constant__ PeerMaps peers) {
-    using C = GemmCfg<kCtaGroup, kSubM>;
+    using C = GemmCfg<kCtaGroup, kSubM, kTileN>;
+    // This instantiation's tile width (shadows the namespace-wide 256).
+    constexpr int kBN = kTileN;
+    constexpr int kTmemCols = 2 * kBN;
+    static_assert(!kStreamK || kTileN == b200::kBN, "stream-K runs 256-wide tiles only");
     constexpr int kStages = C::kStages;
     constexpr int kColsPerChunk = kOutF32 ? 32 : 64;  // output columns per 128-byte staging row
     constexpr int kChunks = kBN / kColsPerChunk;
@@ -894,21 +902,29 @@ static const void* kernel_sym_t(bool f32) {
                : reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<G, S, false, K>);
 }
 
-static const void* kernel_sym(int cta_group, int sub_m, bool f32, bool stream_k) {
+static const void* kernel_sym(int cta_group, int sub_m, bool f32, bool stream_k, int tile_n) {
+    if (tile_n == 128)
+        return f32 ? reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<2, 1, true, false, 128>)
+                   : reinterpret_cast<const void*>(&gemm_tn_sm100_kernel<2, 1, false, false, 128>);
     if (cta_group == 1) return stream_k ? kernel_sym_t<1, 1, true>(f32) : kernel_sym_t<1, 1, false>(f32);
     if (sub_m == 2) return kernel_sym_t<2, 2, false>(f32);
     return stream_k ? kernel_sym_t<2, 1, true>(f32) : kernel_sym_t<2, 1, false>(f32);
 }
 
-static int smem_bytes_for(int cta_group, int sub_m) {
+static int smem_bytes_for(int cta_group, int sub_m, int tile_n) {
+    if (tile_n == 128) return GemmCfg<2, 1, 128>::kSmemBytes;
     if (cta_group == 1) return GemmCfg<1, 1>::kSmemBytes;
     return sub_m == 2 ? GemmCfg<2, 2>::kSmemBytes : GemmCfg<2, 1>::kSmemBytes;
 }
 
-static int stages_for(int cta_group, int sub_m) {
+static int stages_for(int cta_group, int sub_m, int tile_n) {
+    if (tile_n == 128) return GemmCfg<2, 1, 128>::kStages;
     if (cta_group == 1) return GemmCfg<1, 1>::kStages;
     return sub_m == 2 ? GemmCfg<2, 2>::kStages : GemmCfg<2, 1>::kStages;
 }
+
+// Columns of D per tile for a resolved mode.
+static int tile_n_for(int resolved_mode) { return resolved_mode == B200_MODE_2CTA_N128 ? 128 : kBN; }
 
 }  // namespace b200
 
@@ -917,6 +933,7 @@ struct B200Plan {
     cudaStream_t stream = nullptr;
     int cta_group = 1;
     int sub_m = 1;  // 128-row accumulators per CTA per tile
+    int tile_n = 256;  // columns of D per tile
     bool pdl = false;  // launch with programmatic stream serialization
     bool out_f32 = false;
     CUtensorMap tmA{}, tmB{}, tmD{};
@@ -1003,8 +1020,8 @@ static int check_shape(int64_t m, int64_t n, int64_t k, int64_t ldd, int out_dty
         return B200_ERR_INVALID_ARGUMENT;
     }
     if (mode != B200_MODE_AUTO && mode != B200_MODE_1CTA && mode != B200_MODE_2CTA &&
-        mode != B200_MODE_2CTA_M512) {
-        set_error("mode=%d is not one of AUTO(0), 1CTA(1), 2CTA(2), 2CTA_M512(3)", mode);
+        mode != B200_MODE_2CTA_M512 && mode != B200_MODE_2CTA_N128) {
+        set_error("mode=%d is not one of AUTO(0), 1CTA(1), 2CTA(2), 2CTA_M512(3), 2CTA_N128(4)", mode);
         return B200_ERR_INVALID_ARGUMENT;
     }
     if (m < 0 || n < 0 || k < 0) {
@@ -1178,6 +1195,7 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
     const int resolved = resolve_mode(mode, m, n, props.sm_count);
     plan->cta_group = resolved == B200_MODE_1CTA ? 1 : 2;
     plan->sub_m = resolved == B200_MODE_2CTA_M512 ? 2 : 1;
+    plan->tile_n = tile_n_for(resolved);
     plan->empty_problem = empty;
     // Programmatic dependent launch: on unless B200_PDL=0.
     plan->pdl = true;
@@ -1189,7 +1207,7 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
     p.n = static_cast<int>(n);
     p.k = static_cast<int>(k);
     p.num_m_blocks = static_cast<int>((m + tile_m - 1) / tile_m);
-    p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
+    p.num_n_blocks = static_cast<int>((n + plan->tile_n - 1) / plan->tile_n);
     p.num_k_blocks = static_cast<int>((k + kBK - 1) / kBK);
     p.num_tiles = p.num_m_blocks * p.num_n_blocks;
     raster_for(p, tile_m, plan->sub_m, &p.group_m, &p.raster_n);
@@ -1202,7 +1220,7 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
                             kRowsPerCta * plan->sub_m, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc == B200_OK)
             rc = encode_tmap_2d(&plan->tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, n, k, k,
-                                kBN / plan->cta_group, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+                                plan->tile_n / plan->cta_group, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc == B200_OK) {
             if (plan->out_f32)
                 rc = encode_tmap_2d(&plan->tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, m, n, ldd, 32,
@@ -1215,8 +1233,8 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
             delete plan;
             return rc;
         }
-        plan->smem = smem_bytes_for(plan->cta_group, plan->sub_m);
-        const void* sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, false);
+        plan->smem = smem_bytes_for(plan->cta_group, plan->sub_m, plan->tile_n);
+        const void* sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, false, plan->tile_n);
         err = cudaFuncSetAttribute(sym, cudaFuncAttributeMaxDynamicSharedMemorySize, plan->smem);
         if (err == cudaSuccess && plan->cta_group == 2)
             err = cudaFuncSetAttribute(sym, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
@@ -1228,9 +1246,9 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
         const int clusters = std::min(p.num_tiles, slots);
         plan->grid = clusters * plan->cta_group;
         p.kserp_wave = kserp_wave_for(clusters);
-        if (stream_k_layout(p, slots, plan->sub_m)) {
+        if (plan->tile_n == kBN && stream_k_layout(p, slots, plan->sub_m)) {
             plan->grid = p.sk_groups * p.sk_lanes * plan->cta_group;
-            const void* sk_sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, true);
+            const void* sk_sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, true, kBN);
             err = cudaFuncSetAttribute(sk_sym, cudaFuncAttributeMaxDynamicSharedMemorySize, plan->smem);
             if (err == cudaSuccess && plan->cta_group == 2)
                 err = cudaFuncSetAttribute(sk_sym, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
@@ -1285,14 +1303,14 @@ static int plan_create(int64_t m, int64_t n, int64_t k, const void* a, const voi
     info.mode = resolved;
     info.cta_group = plan->cta_group;
     info.tile_m = tile_m;
-    info.tile_n = kBN;
+    info.tile_n = plan->tile_n;
     info.tile_k = kBK;
-    info.stages = stages_for(plan->cta_group, plan->sub_m);
+    info.stages = stages_for(plan->cta_group, plan->sub_m, plan->tile_n);
     info.cluster_m = plan->cta_group;
     info.grid_ctas = plan->grid;
     info.threads_per_cta = kThreads;
     info.smem_bytes = plan->smem;
-    info.tmem_columns = kTmemCols;
+    info.tmem_columns = 2 * plan->tile_n;
     info.num_tiles = empty ? 0 : p.num_tiles;
     info.sm_count = props.sm_count;
     info.device = device;
@@ -1330,7 +1348,12 @@ static int plan_launch(B200Plan* plan, cudaStream_t stream) {
     cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<G, S, F, K>, plan->tmA, plan->tmB, plan->tmD, plan->params, \
                        plan->peer_maps)
     const bool sk = plan->params.sk_iters > 0;
-    if (plan->cta_group == 1 && sk)
+    if (plan->tile_n == 128)
+        err = plan->out_f32 ? cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<2, 1, true, false, 128>, plan->tmA,
+                                                 plan->tmB, plan->tmD, plan->params, plan->peer_maps)
+                            : cudaLaunchKernelEx(&cfg, gemm_tn_sm100_kernel<2, 1, false, false, 128>, plan->tmA,
+                                                 plan->tmB, plan->tmD, plan->params, plan->peer_maps);
+    else if (plan->cta_group == 1 && sk)
         err = plan->out_f32 ? B200_LAUNCH(1, 1, true, true) : B200_LAUNCH(1, 1, false, true);
     else if (plan->cta_group == 1)
         err = plan->out_f32 ? B200_LAUNCH(1, 1, true, false) : B200_LAUNCH(1, 1, false, false);
@@ -1520,25 +1543,26 @@ int b200_gemm_policy(int64_t m, int64_t n, int64_t k, int mode, int sm_count, B2
     const int cta_group = resolved == B200_MODE_1CTA ? 1 : 2;
     const int sub_m = resolved == B200_MODE_2CTA_M512 ? 2 : 1;
     const int tile_m = b200::kRowsPerCta * sub_m * cta_group;
+    const int tile_n = b200::tile_n_for(resolved);
     b200::GemmParams p{};
     p.m = static_cast<int>(m);
     p.n = static_cast<int>(n);
     p.k = static_cast<int>(k);
     p.num_m_blocks = static_cast<int>((m + tile_m - 1) / tile_m);
-    p.num_n_blocks = static_cast<int>((n + b200::kBN - 1) / b200::kBN);
+    p.num_n_blocks = static_cast<int>((n + tile_n - 1) / tile_n);
     p.num_k_blocks = static_cast<int>((k + b200::kBK - 1) / b200::kBK);
     p.num_tiles = p.num_m_blocks * p.num_n_blocks;
     b200::raster_for(p, tile_m, sub_m, &p.group_m, &p.raster_n);
     const int slots = cta_group == 1 ? sm_count : sm_count / 2;
     const int clusters = std::min(p.num_tiles, slots);
     int grid = clusters * cta_group;
-    const bool sk = b200::stream_k_layout(p, slots, sub_m);
+    const bool sk = tile_n == b200::kBN && b200::stream_k_layout(p, slots, sub_m);
     if (sk) grid = p.sk_groups * p.sk_lanes * cta_group;
     B200PolicyInfo& o = *out;
     std::memset(&o, 0, sizeof(o));
     o.mode = resolved;
     o.tile_m = tile_m;
-    o.tile_n = b200::kBN;
+    o.tile_n = tile_n;
     o.num_m_blocks = p.num_m_blocks;
     o.num_n_blocks = p.num_n_blocks;
     o.num_k_blocks = p.num_k_blocks;
@@ -1663,6 +1687,7 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
     const int resolved = resolve_mode(mode, m, n, props.sm_count);
     plan->cta_group = resolved == B200_MODE_1CTA ? 1 : 2;
     plan->sub_m = resolved == B200_MODE_2CTA_M512 ? 2 : 1;
+    plan->tile_n = tile_n_for(resolved);
     plan->empty_problem = (m == 0 || n == 0);
     plan->d_status = status;
     const int tile_m = kRowsPerCta * plan->sub_m * plan->cta_group;
@@ -1671,7 +1696,7 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
     p.n = static_cast<int>(n);
     p.k = static_cast<int>(k);
     p.num_m_blocks = static_cast<int>((m + tile_m - 1) / tile_m);
-    p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
+    p.num_n_blocks = static_cast<int>((n + plan->tile_n - 1) / plan->tile_n);
     p.num_k_blocks = static_cast<int>((k + kBK - 1) / kBK);
     p.num_tiles = p.num_m_blocks * p.num_n_blocks;
     raster_for(p, tile_m, plan->sub_m, &p.group_m, &p.raster_n);
@@ -1683,7 +1708,7 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
                             kRowsPerCta * plan->sub_m, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc == B200_OK)
         rc = encode_tmap_2d(&plan->tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, n, k, k,
-                            kBN / plan->cta_group, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+                            plan->tile_n / plan->cta_group, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc == B200_OK)
         rc = plan->out_f32
                  ? encode_tmap_2d(&plan->tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, m, n, ldd, 32, 32,
@@ -1691,8 +1716,8 @@ static int noalloc_prepare(B200Plan* plan, int64_t m, int64_t n, int64_t k, cons
                  : encode_tmap_2d(&plan->tmD, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, m, n, ldd, 32, 64,
                                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != B200_OK) return rc;
-    plan->smem = smem_bytes_for(plan->cta_group, plan->sub_m);
-    const void* sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, false);
+    plan->smem = smem_bytes_for(plan->cta_group, plan->sub_m, plan->tile_n);
+    const void* sym = kernel_sym(plan->cta_group, plan->sub_m, plan->out_f32, false, plan->tile_n);
     B200_CUDA_TRY(cudaFuncSetAttribute(sym, cudaFuncAttributeMaxDynamicSharedMemorySize, plan->smem));
     if (plan->cta_group == 2)
         B200_CUDA_TRY(cudaFuncSetAttribute(sym, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));

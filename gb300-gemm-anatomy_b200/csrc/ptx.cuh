@@ -426,6 +426,7 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
 
 static_assert(idesc_bf16_f32(128, 256) == 0x08400490u, "idesc M128 N256");
 static_assert(idesc_bf16_f32(256, 256) == 0x10400490u, "idesc M256 N256");
+static_assert(idesc_bf16_f32(256, 128) == 0x10200490u, "idesc M256 N128");
 
 // fp32 pair -> packed bf16x2 (round to nearest even); low half = first value.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

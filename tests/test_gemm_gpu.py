@@ -31,7 +31,7 @@ def maxabs(t):
     return float(t.float().abs().max()) if t.numel() else 0.0
 
 
-@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512"])
+@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512", "2cta_n128"])
 @pytest.mark.parametrize("shape", [(128, 256, 64), (96, 80, 72), (200, 264, 136), (256, 512, 256)])
 def test_small_golden(golden_dir, shape, mode):
     z = np.load(golden_dir / "gemm_small.npz")
@@ -48,7 +48,7 @@ def test_small_golden(golden_dir, shape, mode):
     assert float((d32.double() - ref64).abs().max()) <= 2.0 ** -20 * shape[2]
 
 
-@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512", "auto"])
+@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512", "2cta_n128", "auto"])
 def test_c1_512(golden_dir, mode):
     g = json.loads((golden_dir / "gemm_512.json").read_text())
     a, b = operands.uniform_operands(512, 512, 512, seed=0)
@@ -66,7 +66,7 @@ def test_c1_512(golden_dir, mode):
 @pytest.mark.parametrize("shape", [(1, 8, 8), (17, 24, 8), (129, 264, 72), (300, 1000, 520),
                                    (640, 136, 4104), (1000, 16, 64), (1100, 520, 200),
                                    (384, 104, 256), (384, 128, 64), (2048, 64, 512)])
-@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512"])
+@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512", "2cta_n128"])
 def test_ragged_shapes(shape, mode):
     m, n, k = shape
     a, b = operands.uniform_operands(m, n, k, seed=3)
@@ -94,7 +94,7 @@ def test_ref_compat_exact(golden_dir):
     a = torch.from_numpy(z["a"]).view(torch.bfloat16)
     b = torch.from_numpy(z["b"]).view(torch.bfloat16)
     ref = torch.from_numpy(z["d"])
-    for mode in ("1cta", "2cta", "2cta_m512"):
+    for mode in ("1cta", "2cta", "2cta_m512", "2cta_n128"):
         d = run(a, b, torch.float32, mode)
         max_abs, _ = check.validate_result("ref_compat", ref, d)
         assert max_abs == 0.0
@@ -154,7 +154,7 @@ def test_unaligned_pitch_rejected():
     assert ok
 
 
-@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512"])
+@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512", "2cta_n128"])
 @pytest.mark.parametrize("n", [16, 64, 104, 128, 192])
 def test_narrow_n_strided_repeat(mode, n):
     """Output narrower than one 256-column tile (some 64-column chunks fall
@@ -171,7 +171,7 @@ def test_narrow_n_strided_repeat(mode, n):
         assert bool((host[:, n:] == 0).all())
 
 
-@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512"])
+@pytest.mark.parametrize("mode", ["1cta", "2cta", "2cta_m512", "2cta_n128"])
 def test_launch_after_producer_kernel_sees_its_writes(mode):
     """Plans launch with programmatic dependent launch: a GEMM that follows a
     kernel writing its operand must still read the new values (no global access

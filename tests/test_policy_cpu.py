@@ -82,12 +82,15 @@ def test_environment_overrides(monkeypatch):
 def test_explicit_modes_and_invalid_arguments():
     assert pol(8192, 8192, 8192, mode="1cta")["tile_m"] == 128
     assert pol(8192, 8192, 8192, mode="2cta")["tile_m"] == 256
+    p = pol(4096, 4096, 4096, mode="2cta_n128")  # 512 tiles of 256 x 128, never split along K
+    assert (p["tile_m"], p["tile_n"], p["num_tiles"], p["schedule"]) == (256, 128, 512, "dynamic")
     lib = _lib.load()
     info = _lib.PolicyInfo()
     assert lib.b200_gemm_policy(0, 64, 64, 0, 148, info) == _lib.ERR_INVALID_ARGUMENT
     assert lib.b200_gemm_policy(64, 64, 64, 0, 1, info) == _lib.ERR_INVALID_ARGUMENT
     assert lib.b200_gemm_policy(64, 64, 60, 0, 148, info) == _lib.ERR_UNSUPPORTED  # K % 8
     assert lib.b200_gemm_policy(64, 64, 64, 9, 148, info) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.b200_gemm_policy(64, 64, 64, 5, 148, info) == _lib.ERR_INVALID_ARGUMENT
     assert lib.b200_gemm_policy(64, 64, 64, 0, 148, None) == _lib.ERR_INVALID_ARGUMENT
 
 

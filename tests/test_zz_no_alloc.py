@@ -32,7 +32,8 @@ def _call(fn, a, b, d, mode, stream):
     assert rc == _lib.OK, _lib.last_error()
 
 
-@pytest.mark.parametrize("mode", [_lib.MODE_2CTA, _lib.MODE_1CTA, _lib.MODE_2CTA_M512, _lib.MODE_AUTO])
+@pytest.mark.parametrize("mode", [_lib.MODE_2CTA, _lib.MODE_1CTA, _lib.MODE_2CTA_M512,
+                                  _lib.MODE_2CTA_N128, _lib.MODE_AUTO])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 def test_noalloc_matches_existing_entry_point(mode, out_dtype):
     lib = _lib.load()
