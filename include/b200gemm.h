@@ -65,8 +65,7 @@ enum { B200_OUT_BF16 = 0, B200_OUT_F32 = 1 };
  *              that fill TMEM; 25 % fewer L2->SM bytes per FLOP than 2CTA
  *   2CTA_N128  256 x 128 per CTA pair, double-buffered, 8-slot ring: twice the
  *              tiles of 2CTA (dynamic schedule only). Never chosen by AUTO:
- *              its ring cannot keep enough operand bytes in flight per SM
- *              (measured ~0.7x of 2CTA on B200); kept for experiments
+ *              measured ~0.7x of 2CTA on B200; kept for experiments
  * AUTO picks by shape. */
 enum {
     B200_MODE_AUTO = 0,
